@@ -1,0 +1,348 @@
+// Term-major inverted index built on the GPU from a document-term CSR.
+//
+// Same layout as the reference builder (src/run_correctness_verification.py:32-84):
+// postings grouped by term, ascending doc id inside a term (the stable-sort invariant the
+// chunked path depends on), every list padded to a multiple of 32 entries with doc id -1
+// and weight 0, offsets = exclusive prefix sum of the padded lengths.  The reference does
+// a host argsort; here it is a two-pass counting sort over fixed document blocks:
+//
+//   count : per block b, per term t, how many postings (shared-memory histogram)
+//   scan  : per term, exclusive prefix over blocks -> block_starts[b][t] (kept in the
+//           index: the posting of t at which block b begins), lengths, padded lengths;
+//           then offsets = exclusive scan of the padded lengths
+//   fill  : one warp per block walks its documents in order and appends each posting at
+//           offsets[t] + block_starts[b][t] + (running count of t in b); documents are
+//           visited in ascending order, so every list comes out sorted by doc id.
+#include "common.cuh"
+
+namespace gsp {
+namespace {
+
+constexpr int kCountThreads = 512;
+
+__global__ void __launch_bounds__(kCountThreads)
+count_kernel(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* __restrict__ indptr,
+             const int32_t* __restrict__ indices, uint32_t* __restrict__ counts,
+             int32_t use_smem, int32_t* __restrict__ err) {
+  extern __shared__ uint32_t hist[];
+  const int64_t b = blockIdx.x;
+  const int64_t d0 = b * block_docs;
+  const int64_t d1 = min(d0 + block_docs, n_docs);
+  uint32_t* row = counts + b * int64_t(V);
+  if (use_smem) {
+    for (int32_t t = threadIdx.x; t < V; t += blockDim.x) hist[t] = 0u;
+    __syncthreads();
+  }
+  const int64_t e0 = indptr[d0], e1 = indptr[d1];
+  for (int64_t e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
+    const int32_t t = indices[e];
+    if (t < 0 || t >= V) {
+      atomicExch(err, 1);
+      continue;
+    }
+    if (use_smem) atomicAdd(&hist[t], 1u);
+    else atomicAdd(&row[t], 1u);
+  }
+  if (use_smem) {
+    __syncthreads();
+    for (int32_t t = threadIdx.x; t < V; t += blockDim.x) row[t] = hist[t];
+  }
+}
+
+// per term: exclusive prefix over blocks (in place), lengths, padded lengths
+__global__ void scan_blocks_kernel(int32_t V, int64_t n_blocks, uint32_t* __restrict__ counts,
+                                   uint32_t* __restrict__ block_starts, int32_t* __restrict__ lengths,
+                                   int32_t* __restrict__ padded, int32_t* __restrict__ err) {
+  const int32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= V) return;
+  uint64_t run = 0;
+  uint32_t max_c = 0;
+  for (int64_t b = 0; b < n_blocks; ++b) {
+    const uint32_t c = counts[b * V + t];
+    max_c = max(max_c, c);
+    block_starts[b * V + t] = uint32_t(run);
+    run += c;
+  }
+  block_starts[n_blocks * V + t] = uint32_t(run);
+  if (run > 0x7FFFFFE0ull || max_c > 0xFFFFu) atomicExch(err, 2);
+  lengths[t] = int32_t(run);
+  padded[t] = int32_t((run + kPostingPad - 1) / kPostingPad * kPostingPad);
+}
+
+// One warp per document block; u16 running counts per term in shared memory.
+__global__ void __launch_bounds__(32)
+fill_kernel(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* __restrict__ indptr,
+            const int32_t* __restrict__ indices, const float* __restrict__ data,
+            const int64_t* __restrict__ offsets, const uint32_t* __restrict__ block_starts,
+            int32_t* __restrict__ doc_ids, float* __restrict__ weights) {
+  extern __shared__ uint16_t run16[];
+  const int lane = lane_id();
+  const int64_t b = blockIdx.x;
+  const int64_t d0 = b * block_docs;
+  const int64_t d1 = min(d0 + block_docs, n_docs);
+  const uint32_t* bstart = block_starts + b * int64_t(V);
+  for (int32_t t = lane; t < V; t += 32) run16[t] = 0;
+  __syncwarp();
+  for (int64_t d = d0; d < d1; ++d) {
+    const int64_t e0 = indptr[d], e1 = indptr[d + 1];
+    for (int64_t e = e0; e < e1; e += 32) {
+      const int32_t tr = e + lane < e1 ? indices[e + lane] : -1;
+      const bool live = tr >= 0 && tr < V;   // ids outside [0, V) were rejected by the count pass
+      const int32_t t = live ? tr : -1;
+      const float w = live ? data[e + lane] : 0.0f;
+      // duplicated term ids inside one document keep their CSR order
+      const uint32_t live_mask = __ballot_sync(FULL, live);
+      const uint32_t peers = __match_any_sync(FULL, t) & live_mask;
+      const int rank = __popc(peers & lanemask_lt());
+      const int leader = live ? (__ffs(peers) - 1) : 0;
+      uint32_t old = 0;
+      if (live && rank == 0) {
+        old = run16[t];
+        run16[t] = uint16_t(old + __popc(peers));
+      }
+      old = __shfl_sync(FULL, old, leader);
+      if (live) {
+        const int64_t pos = offsets[t] + int64_t(__ldg(bstart + t)) + old + rank;
+        doc_ids[pos] = int32_t(d);
+        weights[pos] = w;
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// max weight per term (0 for an empty list), one warp per term
+__global__ void max_kernel(int32_t V, const int64_t* __restrict__ offsets,
+                           const int32_t* __restrict__ lengths, const float* __restrict__ weights,
+                           float* __restrict__ max_scores) {
+  const int32_t t = (int32_t)((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int lane = lane_id();
+  if (t >= V) return;
+  const int64_t o = offsets[t];
+  const int32_t L = lengths[t];
+  float m = -INFINITY;
+  for (int32_t p = lane; p < L; p += 32) m = fmaxf(m, weights[o + p]);
+#pragma unroll
+  for (int s = 16; s; s >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, s));
+  if (lane == 0) max_scores[t] = L > 0 ? m : 0.0f;
+}
+
+__global__ void quant_kernel(int32_t V, const int64_t* __restrict__ offsets,
+                             const int32_t* __restrict__ padded, const float* __restrict__ max_scores,
+                             const float* __restrict__ weights, int32_t wdtype, void* out,
+                             float* __restrict__ term_scale) {
+  const int32_t t = (int32_t)((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int lane = lane_id();
+  if (t >= V) return;
+  const int64_t o = offsets[t];
+  const int32_t P = padded[t];
+  if (wdtype == GSP_W_BF16) {
+    __nv_bfloat16* q = static_cast<__nv_bfloat16*>(out);
+    for (int32_t p = lane; p < P; p += 32) q[o + p] = __float2bfloat16_rn(weights[o + p]);
+    return;
+  }
+  uint8_t* q = static_cast<uint8_t*>(out);
+  const float mx = fmaxf(max_scores[t], 0.0f);
+  const float scale = __fdiv_rn(mx, 255.0f);
+  if (lane == 0 && term_scale) term_scale[t] = scale;
+  for (int32_t p = lane; p < P; p += 32) {
+    int v = 0;
+    if (scale > 0.0f) {
+      v = __float2int_rn(__fdiv_rn(weights[o + p], scale));
+      v = min(max(v, 0), 255);
+    }
+    q[o + p] = uint8_t(v);
+  }
+}
+
+__global__ void check_sorted_kernel(int32_t V, const int32_t* __restrict__ doc_ids,
+                                    const int64_t* __restrict__ offsets,
+                                    const int32_t* __restrict__ lengths,
+                                    unsigned long long* __restrict__ n_bad) {
+  const int32_t t = (int32_t)((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int lane = lane_id();
+  if (t >= V) return;
+  const int64_t o = offsets[t];
+  const int32_t L = lengths[t];
+  bool bad = false;
+  for (int32_t p = lane + 1; p < L; p += 32) bad |= doc_ids[o + p] < doc_ids[o + p - 1];
+  if (__any_sync(FULL, bad) && lane == 0) atomicAdd(n_bad, 1ull);
+}
+
+// out[c][t] = offsets[t] + #postings of t with doc id < min(c*chunk, n_docs); one warp per
+// term, binary search per boundary (lists are ascending, the caller checked).
+__global__ void chunk_bounds_kernel(int64_t n_docs, int32_t V, int64_t chunk, int64_t n_chunks,
+                                    const int32_t* __restrict__ doc_ids,
+                                    const int64_t* __restrict__ offsets,
+                                    const int32_t* __restrict__ lengths, int64_t* __restrict__ out) {
+  const int32_t t = (int32_t)((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int lane = lane_id();
+  if (t >= V) return;
+  const int64_t o = offsets[t];
+  const int32_t L = lengths[t];
+  for (int64_t c = lane; c <= n_chunks; c += 32) {
+    const int64_t edge = c < n_chunks ? c * chunk : n_docs;
+    int32_t lo = 0, hi = L;  // first p with doc_ids[o+p] >= edge
+    while (lo < hi) {
+      const int32_t mid = (lo + hi) >> 1;
+      if (int64_t(doc_ids[o + mid]) < edge) lo = mid + 1; else hi = mid;
+    }
+    out[c * V + t] = o + lo;
+  }
+}
+
+int64_t n_blocks_of(int64_t n_docs, int32_t block_docs) {
+  return (n_docs + block_docs - 1) / block_docs;
+}
+
+}  // namespace
+}  // namespace gsp
+
+using namespace gsp;
+
+// workspace: counts [n_blocks * V] u32 | err int32 | scan ws
+extern "C" int64_t gsp_index_ws_bytes(int64_t n_docs, int32_t V, int32_t block_docs) {
+  if (n_docs < 0 || V <= 0 || block_docs <= 0) return -1;
+  const int64_t nb = n_blocks_of(n_docs, block_docs);
+  int64_t bytes = ((nb * V * 4 + 255) / 256) * 256 + 256;
+  bytes += gsp_scan_ws_bytes(V);
+  return bytes;
+}
+
+static int check_csr_args(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* indptr) {
+  GSP_REQUIRE(n_docs >= 0 && V > 0 && block_docs > 0 && block_docs <= 65536 && indptr, GSP_ERR_ARG,
+              "index build: bad arguments (n_docs=%lld V=%d block_docs=%d)", (long long)n_docs, V,
+              block_docs);
+  GSP_REQUIRE(n_docs < 0x7FFFFFFFll, GSP_ERR_UNSUPPORTED, "index build: n_docs must be < 2^31");
+  return GSP_OK;
+}
+
+extern "C" int gsp_index_count(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* indptr,
+                               const int32_t* indices, int32_t* lengths, int32_t* padded,
+                               int64_t* offsets, uint32_t* block_starts, int64_t* total_padded,
+                               void* ws, int64_t ws_bytes, void* stream) {
+  int rc = check_csr_args(n_docs, V, block_docs, indptr);
+  if (rc) return rc;
+  GSP_REQUIRE(ws_bytes >= gsp_index_ws_bytes(n_docs, V, block_docs), GSP_ERR_ARG,
+              "gsp_index_count: workspace too small");
+  cudaStream_t st = as_stream(stream);
+  const int64_t nb = n_blocks_of(n_docs, block_docs);
+  char* w = static_cast<char*>(ws);
+  uint32_t* counts = reinterpret_cast<uint32_t*>(w);
+  int32_t* err = reinterpret_cast<int32_t*>(w + ((nb * V * 4 + 255) / 256) * 256);
+  void* scan_ws = w + ((nb * V * 4 + 255) / 256) * 256 + 256;
+  GSP_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), st));
+  if (nb > 0) {
+    const size_t smem = size_t(V) * 4;
+    const int use_smem = smem <= size_t(max_smem_optin()) ? 1 : 0;
+    if (use_smem) {
+      GSP_CUDA(cudaFuncSetAttribute(count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(smem)));
+    } else {
+      GSP_CUDA(cudaMemsetAsync(counts, 0, size_t(nb) * V * 4, st));
+    }
+    count_kernel<<<unsigned(nb), kCountThreads, use_smem ? smem : 0, st>>>(
+        n_docs, V, block_docs, indptr, indices, counts, use_smem, err);
+    GSP_CHECK_LAUNCH();
+  }
+  scan_blocks_kernel<<<unsigned((V + 255) / 256), 256, 0, st>>>(V, nb, counts, block_starts, lengths,
+                                                                padded, err);
+  GSP_CHECK_LAUNCH();
+  rc = gsp_scan_i32(padded, V, offsets, scan_ws, gsp_scan_ws_bytes(V), stream);
+  if (rc) return rc;
+  // offsets has V+1 slots' worth only when the caller passes V+1; read the total from the
+  // last offset plus the last padded length instead
+  int64_t last_off = 0;
+  int32_t last_pad = 0, herr = 0;
+  GSP_CUDA(cudaMemcpyAsync(&last_off, offsets + (V - 1), sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+  GSP_CUDA(cudaMemcpyAsync(&last_pad, padded + (V - 1), sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  GSP_CUDA(cudaMemcpyAsync(&herr, err, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  GSP_CUDA(cudaStreamSynchronize(st));
+  GSP_REQUIRE(herr != 1, GSP_ERR_ARG, "index build: a column id is outside [0, %d)", V);
+  GSP_REQUIRE(herr != 2, GSP_ERR_UNSUPPORTED,
+              "index build: a posting list exceeds 2^31 entries or a term repeats more than "
+              "65535 times inside one document block");
+  *total_padded = last_off + last_pad;
+  return GSP_OK;
+}
+
+extern "C" int gsp_index_fill(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* indptr,
+                              const int32_t* indices, const float* data, const int64_t* offsets,
+                              const int32_t* lengths, const uint32_t* block_starts,
+                              int64_t total_padded, int32_t* doc_ids, float* weights,
+                              float* max_scores, void* ws, int64_t ws_bytes, void* stream) {
+  int rc = check_csr_args(n_docs, V, block_docs, indptr);
+  if (rc) return rc;
+  (void)ws;
+  (void)ws_bytes;
+  cudaStream_t st = as_stream(stream);
+  const int64_t nb = n_blocks_of(n_docs, block_docs);
+  if (total_padded > 0) {
+    GSP_CUDA(cudaMemsetAsync(doc_ids, 0xFF, size_t(total_padded) * 4, st));
+    GSP_CUDA(cudaMemsetAsync(weights, 0, size_t(total_padded) * 4, st));
+  }
+  if (nb > 0) {
+    const size_t smem = size_t(V) * 2;
+    GSP_REQUIRE(smem <= size_t(max_smem_optin()), GSP_ERR_UNSUPPORTED,
+                "index build: vocabulary %d too large", V);
+    GSP_CUDA(cudaFuncSetAttribute(fill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    fill_kernel<<<unsigned(nb), 32, smem, st>>>(n_docs, V, block_docs, indptr, indices, data, offsets,
+                                                block_starts, doc_ids, weights);
+    GSP_CHECK_LAUNCH();
+  }
+  max_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, st>>>(V, offsets, lengths, weights,
+                                                                       max_scores);
+  GSP_CHECK_LAUNCH();
+  return GSP_OK;
+}
+
+extern "C" int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t* offsets,
+                                  const int32_t* padded, const float* max_scores,
+                                  const float* weights, int32_t wdtype, void* out_weights,
+                                  float* term_scale, void* stream) {
+  GSP_REQUIRE(V > 0 && total_padded >= 0 && (wdtype == GSP_W_BF16 || wdtype == GSP_W_U8) &&
+                  out_weights && (wdtype != GSP_W_U8 || term_scale),
+              GSP_ERR_ARG, "gsp_index_quantize: bad arguments");
+  quant_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, as_stream(stream)>>>(
+      V, offsets, padded, max_scores, weights, wdtype, out_weights, term_scale);
+  GSP_CHECK_LAUNCH();
+  return GSP_OK;
+}
+
+extern "C" int gsp_check_sorted(int32_t V, const int32_t* doc_ids, const int64_t* offsets,
+                                const int32_t* lengths, int64_t* n_bad, void* stream) {
+  GSP_REQUIRE(V > 0 && doc_ids && offsets && lengths && n_bad, GSP_ERR_ARG,
+              "gsp_check_sorted: bad arguments");
+  cudaStream_t st = as_stream(stream);
+  unsigned long long* d_bad = nullptr;
+  GSP_CUDA(cudaMallocAsync(&d_bad, sizeof(unsigned long long), st));
+  GSP_CUDA(cudaMemsetAsync(d_bad, 0, sizeof(unsigned long long), st));
+  check_sorted_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, st>>>(V, doc_ids, offsets,
+                                                                                 lengths, d_bad);
+  GSP_CHECK_LAUNCH();
+  unsigned long long h = 0;
+  GSP_CUDA(cudaMemcpyAsync(&h, d_bad, sizeof(h), cudaMemcpyDeviceToHost, st));
+  GSP_CUDA(cudaFreeAsync(d_bad, st));
+  GSP_CUDA(cudaStreamSynchronize(st));
+  *n_bad = int64_t(h);
+  return GSP_OK;
+}
+
+extern "C" int gsp_chunk_bounds(int64_t n_docs, int32_t V, int64_t doc_chunk, const int32_t* doc_ids,
+                                const int64_t* offsets, const int32_t* lengths, int64_t* out,
+                                void* stream) {
+  GSP_REQUIRE(n_docs >= 0 && V > 0 && doc_chunk > 0 && out, GSP_ERR_ARG,
+              "gsp_chunk_bounds: bad arguments");
+  int64_t n_bad = 0;
+  int rc = gsp_check_sorted(V, doc_ids, offsets, lengths, &n_bad, stream);
+  if (rc) return rc;
+  GSP_REQUIRE(n_bad == 0, GSP_ERR_UNSORTED,
+              "%lld posting lists are not ascending in doc_id. Chunked scoring requires "
+              "ascending lists; otherwise results are silently wrong.",
+              (long long)n_bad);
+  const int64_t n_chunks = (n_docs + doc_chunk - 1) / doc_chunk;
+  chunk_bounds_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, as_stream(stream)>>>(
+      n_docs, V, doc_chunk, n_chunks, doc_ids, offsets, lengths, out);
+  GSP_CHECK_LAUNCH();
+  return GSP_OK;
+}

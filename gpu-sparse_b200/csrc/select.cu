@@ -1,0 +1,270 @@
+// Exact top-k selection over packed candidate keys (sm_100a).
+//
+// A candidate is one uint64: fkey(score) << 32 | (0xFFFFFFFF - doc id).  Larger keys are
+// better (higher score, then lower doc id), and keys of one query are distinct, so "the k
+// largest keys" is exactly the reference's top-k with deterministic tie-breaking.
+//
+// merge_kernel: one CTA per query.  Radix-select the k-th largest key over the query's R
+// candidate lists (8-bit digits, most significant first, shared-memory histogram with
+// warp-aggregated increments, early exit once the boundary bucket is taken whole), gather
+// the k keys at or above the boundary into shared memory, bitonic-sort them descending
+// and decode (score, doc id).  This replaces torch.topk over the dense matrix
+// (src/triton_kernel.py:199), the running cat/topk/gather merge
+// (src/triton_kernel_chunked.py:162-168) and the host-side shard merge
+// (src/comprehensive_benchmark.py:472-480).
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace gsp {
+
+constexpr int kMergeThreads = 512;
+constexpr int kMaxParamCounts = 64;
+constexpr int kMaxK = 8192;
+
+struct CountsParam {
+  int32_t c[kMaxParamCounts];
+};
+
+namespace {
+
+__device__ __forceinline__ int32_t list_count(int32_t b, int32_t r, const int32_t* counts_dev,
+                                              int64_t cstride_b, const CountsParam& cp, bool use_param) {
+  return use_param ? cp.c[r] : counts_dev[int64_t(b) * cstride_b + r];
+}
+
+__global__ void __launch_bounds__(kMergeThreads)
+merge_kernel(const uint64_t* __restrict__ keys, int64_t stride_b, int64_t stride_r, int32_t R,
+             const int32_t* __restrict__ counts_dev, int64_t cstride_b, const CountsParam cp,
+             int32_t use_param, int32_t k, int32_t k_out, int32_t kpow2, int64_t pad_id,
+             float* __restrict__ out_s, int64_t* __restrict__ out_i, uint64_t* __restrict__ out_k) {
+  extern __shared__ uint64_t sk[];
+  __shared__ uint32_t hist[256];
+  __shared__ int32_t s_total, s_n, s_D, s_above, s_cD;
+  const int32_t b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const uint64_t* __restrict__ kb = keys + int64_t(b) * stride_b;
+  const bool up = use_param != 0;
+
+  if (tid == 0) {
+    int32_t tot = 0;
+    for (int32_t r = 0; r < R; ++r) tot += list_count(b, r, counts_dev, cstride_b, cp, up);
+    s_total = tot;
+    s_n = 0;
+  }
+  __syncthreads();
+  const int32_t total = s_total;
+  const int32_t kk = min(k, total);
+
+  uint64_t prefix = 0;
+  if (kk > 0 && kk < total) {
+    int32_t need = kk;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+      for (int j = tid; j < 256; j += blockDim.x) hist[j] = 0u;
+      __syncthreads();
+      const uint64_t pmask = shift == 56 ? 0ull : (~0ull << (shift + 8));
+      for (int32_t r = 0; r < R; ++r) {
+        const int32_t cnt = list_count(b, r, counts_dev, cstride_b, cp, up);
+        const uint64_t* __restrict__ kr = kb + int64_t(r) * stride_r;
+        for (int32_t i0 = 0; i0 < cnt; i0 += blockDim.x) {
+          const int32_t i = i0 + tid;
+          const uint64_t key = i < cnt ? kr[i] : 0ull;
+          const bool live = i < cnt && (key & pmask) == prefix;
+          const uint32_t dig = live ? uint32_t((key >> shift) & 255u) : 0x100u;
+          const uint32_t peers = __match_any_sync(FULL, dig);
+          if (live && (peers & lanemask_lt()) == 0u) atomicAdd(&hist[dig], uint32_t(__popc(peers)));
+        }
+      }
+      __syncthreads();
+      if (wid == 0) {
+        int32_t s = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += int32_t(hist[255 - 8 * lane - j]);
+        int32_t incl = s;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int32_t y = __shfl_up_sync(FULL, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const uint32_t hit = __ballot_sync(FULL, incl >= need);
+        const int L = __ffs(hit) - 1;
+        if (lane == L) {
+          int32_t above = incl - s;
+          for (int j = 0; j < 8; ++j) {
+            const int bin = 255 - 8 * lane - j;
+            const int32_t c = int32_t(hist[bin]);
+            if (above + c >= need) {
+              s_D = bin;
+              s_cD = c;
+              s_above = above;
+              break;
+            }
+            above += c;
+          }
+        }
+      }
+      __syncthreads();
+      need -= s_above;
+      prefix |= uint64_t(s_D) << shift;
+      const bool done = s_cD == need;
+      __syncthreads();
+      if (done) break;
+    }
+  }
+
+  // gather the kk keys >= prefix (all keys when kk == total)
+  for (int32_t r = 0; r < R && kk > 0; ++r) {
+    const int32_t cnt = list_count(b, r, counts_dev, cstride_b, cp, up);
+    const uint64_t* __restrict__ kr = kb + int64_t(r) * stride_r;
+    for (int32_t i0 = 0; i0 < cnt; i0 += blockDim.x) {
+      const int32_t i = i0 + tid;
+      const uint64_t key = i < cnt ? kr[i] : 0ull;
+      const bool keep = i < cnt && key >= prefix;
+      const uint32_t bal = __ballot_sync(FULL, keep);
+      int32_t base = 0;
+      if (lane == 0 && bal) base = atomicAdd(&s_n, __popc(bal));
+      base = __shfl_sync(FULL, base, 0);
+      if (keep) {
+        const int32_t slot = base + __popc(bal & lanemask_lt());
+        if (slot < kpow2) sk[slot] = key;
+      }
+    }
+  }
+  __syncthreads();
+  const int32_t n = min(s_n, kpow2);
+  for (int32_t i = n + tid; i < kpow2; i += blockDim.x) sk[i] = 0ull;
+  __syncthreads();
+  // bitonic sort, descending
+  for (int32_t size = 2; size <= kpow2; size <<= 1) {
+    for (int32_t stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int32_t i = tid; i < kpow2; i += blockDim.x) {
+        const int32_t j = i ^ stride;
+        if (j > i) {
+          const uint64_t a = sk[i], c = sk[j];
+          const bool desc = (i & size) == 0;
+          if ((a < c) == desc) {
+            sk[i] = c;
+            sk[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const int64_t ob = int64_t(b) * k_out;
+  for (int32_t j = tid; j < k_out; j += blockDim.x) {
+    if (j < kk && j < n) {
+      const uint64_t key = sk[j];
+      out_s[ob + j] = key_score(key);
+      out_i[ob + j] = int64_t(key_doc(key));
+      if (out_k) out_k[ob + j] = key;
+    } else {
+      out_s[ob + j] = -INFINITY;
+      out_i[ob + j] = pad_id;
+      if (out_k) out_k[ob + j] = 0ull;
+    }
+  }
+}
+
+// keys of the entries >= tau[b] of a dense score row, compacted per row (order within a
+// row is irrelevant: the merge sorts them)
+__global__ void compact_rows_kernel(const float* __restrict__ scores, int64_t L, int64_t stride,
+                                    const float* __restrict__ tau, uint64_t* __restrict__ out,
+                                    int32_t* __restrict__ counts) {
+  const int64_t b = blockIdx.y;
+  const float t = tau[b];
+  const float* __restrict__ row = scores + b * stride;
+  uint64_t* __restrict__ o = out + b * L;
+  const int lane = lane_id();
+  for (int64_t i0 = int64_t(blockIdx.x) * blockDim.x; i0 < L; i0 += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i = i0 + threadIdx.x;
+    const float s = i < L ? row[i] : 0.0f;
+    const bool keep = i < L && s >= t;
+    const uint32_t bal = __ballot_sync(FULL, keep);
+    int32_t base = 0;
+    if (lane == 0 && bal) base = atomicAdd(counts + b, __popc(bal));
+    base = __shfl_sync(FULL, base, 0);
+    if (keep) o[base + __popc(bal & lanemask_lt())] = pack_key(s, uint32_t(i));
+  }
+}
+
+}  // namespace
+
+int merge_topk_device(const uint64_t* keys, int64_t B, int64_t R, int64_t stride_b, int64_t stride_r,
+                      const int32_t* counts_dev, int64_t cstride_b, const int32_t* counts_host,
+                      int64_t k, float* out_scores, int64_t* out_ids, uint64_t* out_keys,
+                      cudaStream_t st, int64_t pad_id) {
+  GSP_REQUIRE(B >= 0 && R >= 1 && k >= 0, GSP_ERR_ARG, "merge: bad arguments");
+  GSP_REQUIRE(k <= kMaxK, GSP_ERR_UNSUPPORTED, "merge: k %lld exceeds the supported maximum %d",
+              (long long)k, kMaxK);
+  GSP_REQUIRE(R <= 0x7FFFFFFF, GSP_ERR_ARG, "merge: too many lists");
+  if (B == 0 || k == 0) return GSP_OK;
+  CountsParam cp{};
+  int use_param = 0;
+  if (counts_host) {
+    GSP_REQUIRE(R <= kMaxParamCounts, GSP_ERR_UNSUPPORTED, "merge: at most %d host-counted lists",
+                kMaxParamCounts);
+    for (int64_t r = 0; r < R; ++r) cp.c[r] = counts_host[r];
+    use_param = 1;
+  }
+  int32_t kpow2 = 1;
+  while (kpow2 < k) kpow2 <<= 1;
+  const size_t smem = size_t(kpow2) * 8;
+  GSP_CUDA(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  merge_kernel<<<unsigned(B), kMergeThreads, smem, st>>>(keys, stride_b, stride_r, int32_t(R), counts_dev,
+                                                         cstride_b, cp, use_param, int32_t(k), int32_t(k),
+                                                         kpow2, pad_id, out_scores, out_ids, out_keys);
+  GSP_CHECK_LAUNCH();
+  return GSP_OK;
+}
+
+}  // namespace gsp
+
+using namespace gsp;
+
+extern "C" int gsp_merge_topk(const uint64_t* keys, int64_t B, int64_t R, int64_t stride_b,
+                              int64_t stride_r, const int32_t* counts_host, int64_t k, float* out_scores,
+                              int64_t* out_ids, uint64_t* out_keys, void* stream) {
+  GSP_REQUIRE(keys && counts_host && out_scores && out_ids, GSP_ERR_ARG, "gsp_merge_topk: null argument");
+  int64_t total = 0;
+  for (int64_t r = 0; r < R; ++r) {
+    GSP_REQUIRE(counts_host[r] >= 0, GSP_ERR_ARG,
+                "gsp_merge_topk: count %d of list %lld out of range", counts_host[r], (long long)r);
+    total += counts_host[r];
+  }
+  GSP_REQUIRE(k <= total, GSP_ERR_ARG, "gsp_merge_topk: k %lld exceeds the %lld candidates", (long long)k,
+              (long long)total);
+  return merge_topk_device(keys, B, R, stride_b, stride_r, nullptr, 0, counts_host, k, out_scores,
+                           out_ids, out_keys, as_stream(stream));
+}
+
+extern "C" int64_t gsp_compacted_ws_bytes(int64_t B, int64_t L, int64_t k, int64_t max_cand) {
+  (void)k;
+  (void)max_cand;
+  if (B < 0 || L < 0) return -1;
+  return ((B * L * 8 + 255) / 256) * 256 + ((B * 4 + 255) / 256) * 256;
+}
+
+extern "C" int gsp_compacted_topk(const float* scores, int64_t B, int64_t L, int64_t stride,
+                                  const float* tau, int64_t k, int64_t max_cand, float* out_v,
+                                  int64_t* out_i, void* ws, int64_t ws_bytes, void* stream) {
+  GSP_REQUIRE(B >= 0 && L >= 0 && stride >= L && k >= 0 && max_cand >= 0, GSP_ERR_ARG,
+              "gsp_compacted_topk: bad arguments");
+  GSP_REQUIRE(ws_bytes >= gsp_compacted_ws_bytes(B, L, k, max_cand), GSP_ERR_ARG,
+              "gsp_compacted_topk: workspace too small");
+  const int64_t kk = std::min(k, L);
+  if (B == 0 || kk == 0) return GSP_OK;
+  GSP_REQUIRE(L <= 0x7FFFFFFFll, GSP_ERR_UNSUPPORTED, "gsp_compacted_topk: row too long");
+  cudaStream_t st = as_stream(stream);
+  char* w = static_cast<char*>(ws);
+  uint64_t* keys = reinterpret_cast<uint64_t*>(w);
+  int32_t* counts = reinterpret_cast<int32_t*>(w + ((B * L * 8 + 255) / 256) * 256);
+  GSP_CUDA(cudaMemsetAsync(counts, 0, size_t(B) * 4, st));
+  const int64_t per = 256;
+  int64_t gx = std::min<int64_t>((L + per - 1) / per, 1024);
+  GSP_REQUIRE(B <= 65535, GSP_ERR_UNSUPPORTED, "gsp_compacted_topk: at most 65535 rows per call");
+  compact_rows_kernel<<<dim3(unsigned(gx), unsigned(B)), unsigned(per), 0, st>>>(scores, L, stride, tau,
+                                                                                keys, counts);
+  GSP_CHECK_LAUNCH();
+  return merge_topk_device(keys, B, 1, L, L, counts, 1, nullptr, kk, out_v, out_i, nullptr, st, 0);
+}

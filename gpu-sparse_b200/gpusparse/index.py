@@ -1,0 +1,268 @@
+"""GPU-resident term-major inverted index (src/gpu_inverted_index.py:21-35 layout).
+
+Postings of all terms are concatenated, each list ascending in doc id and padded to a
+multiple of 32 entries (doc id -1, weight 0), so every list starts on a 128-byte boundary
+and 32-wide warp loads of a list are aligned.  Besides the reference's fields the index
+keeps:
+
+* ``weight_dtype`` ("fp32" | "bf16" | "u8") and ``weights_q`` (bf16 or uint8 postings) with
+  ``term_scale`` (uint8 mode: weight = q * term_scale[t]);
+* ``block_starts`` int32 [n_blocks+1, V]: postings of term t with doc id < b*block_docs,
+  the doc-range blocks a scorer uses to start mid-list without searching;
+* ``doc_base``: global id of local document 0 when the index is one doc-range shard.
+
+Builders run on the GPU (csrc/build.cu); the CSR is only copied host -> device.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Optional, Tuple
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+BLOCK_SIZE = 32          # posting lists are padded to a warp (src/gpu_inverted_index.py:18)
+BLOCK_DOCS = 4096        # documents per block_starts row
+VOCAB_SIZE = 30522       # src/run_correctness_verification.py:28
+
+
+@dataclass
+class GPUInvertedIndex:
+    """GPU-resident index with block-aligned posting lists (reference fields first)."""
+    doc_ids: torch.Tensor
+    scores: Optional[torch.Tensor]
+    offsets: torch.Tensor
+    lengths: torch.Tensor
+    padded_lengths: torch.Tensor
+    max_scores: torch.Tensor
+    num_docs: int
+    vocab_size: int
+    device: torch.device
+    weight_dtype: str = "fp32"
+    weights_q: Optional[torch.Tensor] = None
+    term_scale: Optional[torch.Tensor] = None
+    block_starts: Optional[torch.Tensor] = None
+    block_docs: int = BLOCK_DOCS
+    doc_base: int = 0
+    _view: object = field(default=None, repr=False, compare=False)
+
+
+def _dev(device) -> torch.device:
+    d = torch.device(device)
+    if d.type != "cuda":
+        raise RuntimeError("GPUSparse requires a CUDA device; no CPU path exists")
+    if d.index is None:
+        d = torch.device("cuda", torch.cuda.current_device())
+    return d
+
+
+def build_from_csr_tensors(indptr: torch.Tensor, indices: torch.Tensor, data: torch.Tensor,
+                           vocab_size: int, device=None, weight_dtype: str = "fp32",
+                           doc_base: int = 0, keep_fp32: bool = True,
+                           block_docs: int = BLOCK_DOCS) -> GPUInvertedIndex:
+    """Build from device CSR tensors (indptr int64 [N+1], indices int32, data fp32)."""
+    device = _dev(device if device is not None else indptr.device)
+    indptr = indptr.to(device=device, dtype=torch.int64).contiguous()
+    indices = indices.to(device=device, dtype=torch.int32).contiguous()
+    data = data.to(device=device, dtype=torch.float32).contiguous()
+    N = indptr.numel() - 1
+    V = int(vocab_size)
+    if V <= 0:
+        raise ValueError("vocab_size must be positive")
+    lib = L.lib()
+    with torch.cuda.device(device):
+        st = L.stream_of(device)
+        nb = (N + block_docs - 1) // block_docs
+        ws = L.workspace(lib.gsp_index_ws_bytes(N, V, block_docs), device)
+        lengths = torch.empty(V, dtype=torch.int32, device=device)
+        padded = torch.empty(V, dtype=torch.int32, device=device)
+        offsets = torch.empty(V, dtype=torch.int64, device=device)
+        block_starts = torch.empty((nb + 1, V), dtype=torch.int32, device=device)
+        total = ctypes.c_int64(0)
+        L.check(lib.gsp_index_count(N, V, block_docs, L.ptr(indptr), L.ptr(indices),
+                                    L.ptr(lengths), L.ptr(padded), L.ptr(offsets),
+                                    L.ptr(block_starts), ctypes.byref(total), L.ptr(ws),
+                                    ws.numel(), st), "index build")
+        P = int(total.value)
+        doc_ids = torch.empty(max(P, 0), dtype=torch.int32, device=device)
+        scores = torch.empty(max(P, 0), dtype=torch.float32, device=device)
+        max_scores = torch.empty(V, dtype=torch.float32, device=device)
+        L.check(lib.gsp_index_fill(N, V, block_docs, L.ptr(indptr), L.ptr(indices), L.ptr(data),
+                                   L.ptr(offsets), L.ptr(lengths), L.ptr(block_starts), P,
+                                   L.ptr(doc_ids), L.ptr(scores), L.ptr(max_scores), L.ptr(ws),
+                                   ws.numel(), st), "index build")
+        idx = GPUInvertedIndex(doc_ids=doc_ids, scores=scores, offsets=offsets, lengths=lengths,
+                               padded_lengths=padded, max_scores=max_scores, num_docs=N,
+                               vocab_size=V, device=device, block_starts=block_starts,
+                               block_docs=block_docs, doc_base=int(doc_base))
+        if weight_dtype != "fp32":
+            quantize_(idx, weight_dtype, keep_fp32=keep_fp32)
+    return idx
+
+
+def quantize_(index: GPUInvertedIndex, weight_dtype: str, keep_fp32: bool = True) -> None:
+    """Convert the posting weights to bf16 or uint8-with-per-term-scale in place."""
+    if weight_dtype not in ("bf16", "u8"):
+        raise ValueError(f"weight_dtype must be fp32, bf16 or u8, got {weight_dtype!r}")
+    if index.scores is None:
+        raise ValueError("index has no fp32 weights to quantise")
+    dev = index.device
+    P = index.doc_ids.numel()
+    if weight_dtype == "bf16":
+        q = torch.empty(P, dtype=torch.bfloat16, device=dev)
+        scale = None
+        code = L.W_BF16
+    else:
+        q = torch.empty(P, dtype=torch.uint8, device=dev)
+        scale = torch.empty(index.vocab_size, dtype=torch.float32, device=dev)
+        code = L.W_U8
+    with torch.cuda.device(dev):
+        L.check(L.lib().gsp_index_quantize(index.vocab_size, P, L.ptr(index.offsets),
+                                           L.ptr(index.padded_lengths), L.ptr(index.max_scores),
+                                           L.ptr(index.scores), code, L.ptr(q), L.ptr(scale),
+                                           L.stream_of(dev)), "quantize")
+    index.weights_q, index.term_scale, index.weight_dtype = q, scale, weight_dtype
+    if not keep_fp32:
+        index.scores = None
+    index._view = None
+
+
+def dequantized_weights(index: GPUInvertedIndex) -> torch.Tensor:
+    """fp32 weights the scorer effectively uses (q * scale_t with one fp32 rounding)."""
+    if index.weight_dtype == "fp32":
+        return index.scores
+    if index.weight_dtype == "bf16":
+        return index.weights_q.float()
+    term_of = torch.repeat_interleave(torch.arange(index.vocab_size, device=index.device),
+                                      index.padded_lengths.long())
+    return index.weights_q.float() * index.term_scale[term_of]
+
+
+def ensure_blocks(index: GPUInvertedIndex) -> None:
+    """Derive block_starts for an index constructed without them (e.g. field by field, as
+    the reference's plug-in does); validates that lists ascend (ValueError otherwise)."""
+    if getattr(index, "block_starts", None) is not None:
+        return
+    from .scoring import build_chunk_boundaries
+    bd = getattr(index, "block_docs", None) or BLOCK_DOCS
+    b = build_chunk_boundaries(index, bd)
+    index.block_starts = (b - index.offsets.unsqueeze(0)).to(torch.int32).contiguous()
+    index.block_docs = bd
+
+
+def view(index: GPUInvertedIndex) -> L.IndexView:
+    ensure_blocks(index)
+    wd = getattr(index, "weight_dtype", "fp32")
+    if wd == "fp32":
+        w, code = index.scores, L.W_F32
+    elif wd == "bf16":
+        w, code = index.weights_q, L.W_BF16
+    else:
+        w, code = index.weights_q, L.W_U8
+    v = L.IndexView()
+    v.n_docs = int(index.num_docs)
+    v.doc_base = int(getattr(index, "doc_base", 0))
+    v.V = int(index.vocab_size)
+    v.block_docs = int(index.block_docs)
+    v.wdtype = code
+    v.doc_ids = index.doc_ids.data_ptr()
+    v.weights = w.data_ptr()
+    ts = getattr(index, "term_scale", None)
+    v.term_scale = ts.data_ptr() if ts is not None else 0
+    v.offsets = index.offsets.data_ptr()
+    v.lengths = index.lengths.data_ptr()
+    v.block_starts = index.block_starts.data_ptr()
+    return v
+
+
+# ------------------------------------------------------------------ reference builders
+
+def _csr_to_device(indptr, indices, data, device):
+    device = _dev(device)
+    return (torch.as_tensor(np.ascontiguousarray(indptr, dtype=np.int64)).to(device),
+            torch.as_tensor(np.ascontiguousarray(indices, dtype=np.int32)).to(device),
+            torch.as_tensor(np.ascontiguousarray(data, dtype=np.float32)).to(device))
+
+
+def build_index_from_scipy(csr_mat, device, vocab_size: int, **kw) -> GPUInvertedIndex:
+    csr = csr_mat.tocsr()
+    ip, ix, dt = _csr_to_device(csr.indptr, csr.indices, csr.data, device)
+    return build_from_csr_tensors(ip, ix, dt, vocab_size, device, **kw)
+
+
+def build_gpu_index_from_csr(csr_mat, device, **kw) -> GPUInvertedIndex:
+    """src/run_correctness_verification.py:32-84 (vocabulary fixed at VOCAB_SIZE)."""
+    return build_index_from_scipy(csr_mat, device, VOCAB_SIZE, **kw)
+
+
+def build_gpu_inverted_index(doc_term_ids: list, doc_term_scores: list, vocab_size: int,
+                             device: torch.device = torch.device("cuda:0"),
+                             **kw) -> GPUInvertedIndex:
+    """src/gpu_inverted_index.py:38-113: lists of per-document term ids / scores."""
+    lens = np.fromiter((len(t) for t in doc_term_ids), dtype=np.int64, count=len(doc_term_ids))
+    indptr = np.zeros(len(lens) + 1, dtype=np.int64)
+    np.cumsum(lens, out=indptr[1:])
+    indices = (np.concatenate([np.asarray(t, dtype=np.int64) for t in doc_term_ids])
+               if len(lens) and indptr[-1] else np.zeros(0, dtype=np.int64))
+    data = (np.concatenate([np.asarray(s, dtype=np.float32) for s in doc_term_scores])
+            if len(lens) and indptr[-1] else np.zeros(0, dtype=np.float32))
+    if indices.size and (indices.min() < 0 or indices.max() >= vocab_size):
+        raise IndexError("term id outside [0, vocab_size)")
+    ip, ix, dt = _csr_to_device(indptr, indices.astype(np.int32), data, device)
+    return build_from_csr_tensors(ip, ix, dt, vocab_size, device, **kw)
+
+
+def build_gpu_inverted_index_from_sparse(sparse_matrix: torch.Tensor,
+                                         device: torch.device = torch.device("cuda:0"),
+                                         **kw) -> GPUInvertedIndex:
+    """src/gpu_inverted_index.py:116-134: dense or torch-sparse [num_docs, vocab] matrix;
+    entries that are exactly zero are not postings (np.nonzero semantics)."""
+    m = sparse_matrix.to_dense() if sparse_matrix.is_sparse else sparse_matrix
+    m = m.to(device=_dev(device), dtype=torch.float32)
+    N, V = m.shape
+    nz = m != 0
+    counts = nz.sum(dim=1, dtype=torch.int64)
+    indptr = torch.zeros(N + 1, dtype=torch.int64, device=m.device)
+    torch.cumsum(counts, 0, out=indptr[1:])
+    rows, cols = torch.nonzero(nz, as_tuple=True)      # row-major, columns ascending
+    return build_from_csr_tensors(indptr, cols.to(torch.int32), m[rows, cols], V, device, **kw)
+
+
+def generate_synthetic_splade_data(num_docs: int, vocab_size: int = 30522,
+                                   avg_terms_per_doc: int = 150,
+                                   score_range: Tuple[float, float] = (0.1, 3.0),
+                                   zipf_a: float = 1.5, seed: int = 42) -> Tuple[list, list]:
+    """src/gpu_inverted_index.py:137-174: Zipf(zipf_a) terms without replacement,
+    Poisson(avg) term counts floored at 10, uniform scores, numpy RandomState(seed)."""
+    rng = np.random.RandomState(seed)
+    ranks = np.arange(1, vocab_size + 1, dtype=np.float64)
+    probs = 1.0 / np.power(ranks, zipf_a)
+    probs /= probs.sum()
+    ids, scs = [], []
+    for _ in range(num_docs):
+        n_terms = min(max(10, rng.poisson(avg_terms_per_doc)), vocab_size)
+        terms = rng.choice(vocab_size, size=n_terms, replace=False, p=probs)
+        scores = rng.uniform(score_range[0], score_range[1], size=n_terms).astype(np.float32)
+        ids.append(terms.tolist())
+        scs.append(scores.tolist())
+    return ids, scs
+
+
+def index_memory_stats(index: GPUInvertedIndex) -> dict:
+    """src/gpu_inverted_index.py:177-196 (plus the quantised weights when present)."""
+    def nbytes(t):
+        return 0 if t is None else t.nelement() * t.element_size()
+    doc_ids_bytes = nbytes(index.doc_ids)
+    scores_bytes = nbytes(index.scores) + nbytes(index.weights_q) + nbytes(index.term_scale)
+    meta_bytes = (nbytes(index.offsets) + nbytes(index.lengths) + nbytes(index.padded_lengths)
+                  + nbytes(index.max_scores) + nbytes(index.block_starts))
+    n = int(index.lengths.sum().item())
+    npad = int(index.padded_lengths.sum().item()) if index.padded_lengths is not None else n
+    return {"doc_ids_MB": doc_ids_bytes / 1e6, "scores_MB": scores_bytes / 1e6,
+            "metadata_MB": meta_bytes / 1e6,
+            "total_MB": (doc_ids_bytes + scores_bytes + meta_bytes) / 1e6,
+            "num_postings": n, "num_padded": npad,
+            "padding_overhead": 1.0 - n / max(1, npad)}

@@ -1,0 +1,194 @@
+"""Reference-named scoring API over the sm_100a kernels (drop-in for src/triton_kernel.py,
+src/triton_kernel_chunked.py and src/fused_topk.py).
+
+All three reference scorers (monolithic, chunked, chunked + threshold-compacted) return
+the same exact top-k, so here they share one fused kernel path (csrc/score.cu): a batch
+is scored tile by tile in shared memory and selected on chip, with no [B, N] matrix.
+Their tuning arguments are validated exactly as the reference validates them
+(``block_pl`` must be a positive power of two -> AssertionError; a supplied
+``chunk_bounds`` must have V columns) and otherwise have no effect on the result.
+
+Results: fp32 scores [B, k'] descending and int64 global doc ids [B, k'], k' =
+min(top_k, num_docs), ties broken by ascending doc id, bitwise reproducible.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib as L
+from .index import GPUInvertedIndex, view
+
+
+def _check_block_pl(block_pl: int) -> None:
+    # src/triton_kernel.py:175 (and :276, triton_kernel_chunked.py:135)
+    assert block_pl > 0 and (block_pl & (block_pl - 1)) == 0, \
+        f"block_pl must be a positive power of 2, got {block_pl}"
+
+
+def _prep_queries(index: GPUInvertedIndex, qi: torch.Tensor, qs: torch.Tensor):
+    dev = index.device
+    if qi.dim() != 2 or qs.shape != qi.shape:
+        raise ValueError(f"query tensors must be [B, W] of equal shape, got {tuple(qi.shape)} "
+                         f"and {tuple(qs.shape)}")
+    L.require_cuda(qi, "query_term_ids")
+    L.require_cuda(qs, "query_term_scores")
+    if qi.device != dev or qs.device != dev:
+        raise ValueError(f"query tensors must live on the index device {dev}")
+    if qi.dtype != torch.int32:
+        if qi.dtype.is_floating_point:
+            raise ValueError("query_term_ids must be an integer tensor")
+        V = int(index.vocab_size)
+        qi = torch.where((qi < 0) | (qi >= V), torch.full_like(qi, -1), qi).to(torch.int32)
+    if qs.dtype != torch.float32:
+        qs = qs.to(torch.float32)
+    return qi.contiguous(), qs.contiguous()
+
+
+def score_topk(index: GPUInvertedIndex, query_term_ids: torch.Tensor,
+               query_term_scores: torch.Tensor, top_k: int = 10, with_keys: bool = False,
+               out: Optional[Tuple[torch.Tensor, ...]] = None):
+    """Exact top-k of every query over the whole index (see module docstring).
+
+    with_keys=True also returns the packed uint64 candidate keys (as int64) used by the
+    multi-GPU merge.  ``out`` may pass preallocated (scores, ids[, keys]) tensors.
+    """
+    if top_k < 1:
+        raise ValueError("top_k must be >= 1")
+    qi, qs = _prep_queries(index, query_term_ids, query_term_scores)
+    B, W = qi.shape
+    N = int(index.num_docs)
+    k = min(int(top_k), N)
+    dev = index.device
+    lib = L.lib()
+    with torch.cuda.device(dev):
+        v = view(index)
+        if out is not None:
+            s_out, i_out = out[0], out[1]
+            k_out = out[2] if with_keys else None
+        else:
+            s_out = torch.empty((B, k), dtype=torch.float32, device=dev)
+            i_out = torch.empty((B, k), dtype=torch.int64, device=dev)
+            k_out = torch.empty((B, k), dtype=torch.int64, device=dev) if with_keys else None
+        if B == 0 or k == 0:
+            return (s_out, i_out, k_out) if with_keys else (s_out, i_out)
+        ws_bytes = lib.gsp_score_ws_bytes(ctypes.byref(v), B, max(W, 1), k)
+        if ws_bytes < 0:
+            L.check(int(-ws_bytes), "score_topk")
+        ws = L.workspace(ws_bytes, dev)
+        L.check(lib.gsp_score_topk(ctypes.byref(v), L.ptr(qi), L.ptr(qs), B, max(W, 1), k,
+                                   L.ptr(s_out), L.ptr(i_out), L.ptr(k_out), L.ptr(ws), ws_bytes,
+                                   L.stream_of(dev)), "score_topk")
+    return (s_out, i_out, k_out) if with_keys else (s_out, i_out)
+
+
+def triton_fused_score(index, query_term_ids: torch.Tensor, query_term_scores: torch.Tensor,
+                       top_k: int = 10, block_pl: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """src/triton_kernel.py:159-200 -- exact scoring + top-k (fp32 [B,k'], int64 [B,k'])."""
+    _check_block_pl(block_pl)
+    return score_topk(index, query_term_ids, query_term_scores, top_k)
+
+
+def triton_wand_score(index, query_term_ids: torch.Tensor, query_term_scores: torch.Tensor,
+                      top_k: int = 10, block_pl: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """src/triton_kernel.py:260-307.  The reference's WAND scorer runs with threshold 0
+    (:290) and so prunes nothing; its result is the exhaustive one, returned here."""
+    _check_block_pl(block_pl)
+    return score_topk(index, query_term_ids, query_term_scores, top_k)
+
+
+def build_chunk_boundaries(index, doc_chunk: int) -> torch.Tensor:
+    """src/triton_kernel_chunked.py:83-122: int64 [n_chunks+1, V] posting offsets of
+    every (chunk boundary, term); ValueError if any list is not ascending in doc id."""
+    if doc_chunk <= 0:
+        raise ValueError("doc_chunk must be positive")
+    dev = index.device if isinstance(index.device, torch.device) else torch.device(index.device)
+    N, V = int(index.num_docs), int(index.vocab_size)
+    n_chunks = (N + doc_chunk - 1) // doc_chunk
+    out = torch.empty((n_chunks + 1, V), dtype=torch.int64, device=dev)
+    with torch.cuda.device(dev):
+        L.check(L.lib().gsp_chunk_bounds(N, V, int(doc_chunk), L.ptr(index.doc_ids),
+                                         L.ptr(index.offsets), L.ptr(index.lengths), L.ptr(out),
+                                         L.stream_of(dev)), "build_chunk_boundaries")
+    return out
+
+
+def _check_chunk_bounds(index, chunk_bounds, doc_chunk):
+    if doc_chunk <= 0:
+        raise ValueError("doc_chunk must be positive")
+    if chunk_bounds is None:
+        # the reference derives (and validates) the bounds when none are passed
+        build_chunk_boundaries(index, doc_chunk)
+        return
+    if chunk_bounds.dim() != 2 or chunk_bounds.shape[1] != int(index.vocab_size):
+        raise ValueError(f"chunk_bounds must be [n_chunks+1, V], got {tuple(chunk_bounds.shape)}")
+
+
+def triton_chunked_score(index, query_term_ids, query_term_scores, top_k=10, doc_chunk=131072,
+                         block_pl=128, chunk_bounds=None):
+    """src/triton_kernel_chunked.py:125-170.  Same result as triton_fused_score; the
+    doc-chunking the reference does on the host happens on chip here."""
+    _check_block_pl(block_pl)
+    _check_chunk_bounds(index, chunk_bounds, doc_chunk)
+    return score_topk(index, query_term_ids, query_term_scores, top_k)
+
+
+def triton_chunked_score_fused(index, query_term_ids, query_term_scores, top_k=10,
+                               doc_chunk=131072, block_pl=128, chunk_bounds=None, max_cand=8192):
+    """src/fused_topk.py:106-160.  Threshold-compacted selection is the scorer's own
+    selection here (a running per-query threshold with exact compaction)."""
+    _check_block_pl(block_pl)
+    _check_chunk_bounds(index, chunk_bounds, doc_chunk)
+    if max_cand < 0:
+        raise ValueError("max_cand must be >= 0")
+    return score_topk(index, query_term_ids, query_term_scores, top_k)
+
+
+def compacted_topk(scores: torch.Tensor, tau: torch.Tensor, k: int, max_cand: int = 8192,
+                   block: int = 1024):
+    """src/fused_topk.py:71-103: top-min(k, L) of the entries >= tau[b] of each row of
+    ``scores`` [B, L] (column indices, int64), padded with (-inf, 0) when fewer survive.
+    The answer does not depend on max_cand/block (the reference's overflow fallback makes
+    it exact too); ties break by ascending column."""
+    if scores.dim() != 2:
+        raise ValueError("scores must be [B, L]")
+    L.require_cuda(scores, "scores")
+    B, Lc = scores.shape
+    kk = min(int(k), Lc)
+    dev = scores.device
+    if scores.dtype != torch.float32:
+        scores = scores.float()
+    if scores.stride(1) != 1:
+        scores = scores.contiguous()
+    tau = tau.to(device=dev, dtype=torch.float32).contiguous()
+    if tau.numel() != B:
+        raise ValueError("tau must have one entry per row")
+    v = torch.empty((B, kk), dtype=torch.float32, device=dev)
+    i = torch.empty((B, kk), dtype=torch.int64, device=dev)
+    if B == 0 or kk == 0:
+        return v, i
+    lib = L.lib()
+    with torch.cuda.device(dev):
+        nb = lib.gsp_compacted_ws_bytes(B, Lc, kk, max_cand)
+        ws = L.workspace(nb, dev)
+        L.check(lib.gsp_compacted_topk(L.ptr(scores), B, Lc, scores.stride(0), L.ptr(tau), kk,
+                                       int(max_cand), L.ptr(v), L.ptr(i), L.ptr(ws), nb,
+                                       L.stream_of(dev)), "compacted_topk")
+    return v, i
+
+
+def merge_topk(keys: torch.Tensor, counts, k: int, stride_r: Optional[int] = None):
+    """Exact top-k over R candidate lists per query.  keys: int64 [R, B, kin] packed keys
+    (as returned by score_topk(with_keys=True)), counts: R valid-entry counts."""
+    R, B, kin = keys.shape
+    dev = keys.device
+    cnt = (ctypes.c_int32 * R)(*[int(c) for c in counts])
+    k = int(k)
+    s = torch.empty((B, k), dtype=torch.float32, device=dev)
+    i = torch.empty((B, k), dtype=torch.int64, device=dev)
+    with torch.cuda.device(dev):
+        L.check(L.lib().gsp_merge_topk(L.ptr(keys), B, R, kin, B * kin, cnt, k, L.ptr(s),
+                                       L.ptr(i), None, L.stream_of(dev)), "merge_topk")
+    return s, i

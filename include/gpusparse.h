@@ -1,0 +1,157 @@
+/*
+ * gpusparse.h -- C ABI of the B200 (sm_100a) exact learned-sparse scoring library
+ * (libgpusparse.so).  Plain pointers, sizes and a cudaStream_t passed as void*; no torch
+ * types.  Every entry point returns an int status (GSP_OK = 0); gsp_last_error() returns
+ * a human-readable message for the calling thread's last failure.
+ *
+ * Reference interfaces replaced (paths inside the GPUSparse checkout):
+ *   gsp_index_*           src/run_correctness_verification.py:32-84  build_gpu_index_from_csr
+ *                         lsr_benchmark_engine/gpusparse_retrieval.py:81-115  build_index
+ *                         src/gpu_inverted_index.py:21-35  GPUInvertedIndex layout
+ *   gsp_chunk_bounds      src/triton_kernel_chunked.py:83-122  build_chunk_boundaries
+ *   gsp_score_topk        src/triton_kernel.py:159-200  triton_fused_score
+ *                         src/triton_kernel_chunked.py:125-170  triton_chunked_score
+ *                         src/fused_topk.py:106-160  triton_chunked_score_fused
+ *   gsp_compacted_topk    src/fused_topk.py:71-103  compacted_topk
+ *   gsp_merge_topk        src/comprehensive_benchmark.py:472-480 (host-side shard merge),
+ *                         src/triton_kernel_chunked.py:162-168 (running top-k merge)
+ *   gsp_synth_*           src/gpu_inverted_index.py:137-174  generate_synthetic_splade_data
+ *                         (the seeded SPLADE-shaped law of the benchmark configs)
+ *
+ * Layout of an index on the device (one shard of `n_docs` documents, ids local to it):
+ *   doc_ids      int32 [P_pad]  term-major postings, ascending doc id within a term,
+ *                               each list padded to a multiple of 32 with -1
+ *   weights      fp32 / bf16 / uint8 [P_pad]  (padding weight 0)
+ *   term_scale   fp32 [V]       uint8 mode only: weight = q * term_scale[t]
+ *   offsets      int64 [V]      first posting of term t (a multiple of 32)
+ *   lengths      int32 [V]      real postings of term t
+ *   padded       int32 [V]      lengths rounded up to 32
+ *   max_scores   fp32 [V]       max weight of term t (0 for an empty list)
+ *   block_starts uint32 [n_blocks+1, V]  postings of term t with doc id < b*block_docs
+ */
+#ifndef GPUSPARSE_H
+#define GPUSPARSE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes; the Python wrapper maps them to the reference's exception types */
+#define GSP_OK 0
+#define GSP_ERR_ARG 1          /* ValueError: bad size, pointer, dtype or range        */
+#define GSP_ERR_UNSORTED 2     /* ValueError: a posting list is not ascending          */
+#define GSP_ERR_OVERFLOW 3     /* RuntimeError: a fixed-capacity structure overflowed  */
+#define GSP_ERR_CUDA 4         /* RuntimeError: a CUDA runtime call failed             */
+#define GSP_ERR_TIMEOUT 5      /* RuntimeError: a bounded device wait ran out          */
+#define GSP_ERR_UNSUPPORTED 6  /* RuntimeError: input outside the supported envelope   */
+#define GSP_ERR_BLOCK_PL 7     /* AssertionError: block_pl is not a positive power of 2 */
+
+/* weight dtypes */
+#define GSP_W_F32 0
+#define GSP_W_BF16 1
+#define GSP_W_U8 2
+
+const char* gsp_last_error(void);
+int gsp_version(void);
+
+/* Exclusive prefix sum of n int32 values into int64 out[0..n] (out[n] = total). */
+int gsp_scan_i32(const int32_t* in, int64_t n, int64_t* out, void* ws, int64_t ws_bytes,
+                 void* stream);
+int64_t gsp_scan_ws_bytes(int64_t n);
+
+/* ---------------------------------------------------------------- synthetic data */
+/* Items [first, first+n) of the seeded SPLADE-shaped law (kind 0 = documents,
+ * 1 = queries).  Tables (device, fp64): nnz_cdf[n_nnz] over nnz = nnz_lo.., term_cdf[V],
+ * wtab[65537].  Step 1 writes nnz[n]; the caller scans it into indptr; step 2 fills. */
+int gsp_synth_nnz(uint64_t seed, uint32_t kind, uint64_t first, int64_t n, int32_t V,
+                  const double* nnz_cdf, int32_t n_nnz, int32_t nnz_lo, int32_t min_nnz_item0,
+                  int32_t* nnz, void* stream);
+int gsp_synth_fill(uint64_t seed, uint32_t kind, uint64_t first, int64_t n, int32_t V,
+                   const double* term_cdf, const int32_t* term_guide, const double* wtab,
+                   const int64_t* indptr, int32_t* indices, float* data, void* stream);
+
+/* ---------------------------------------------------------------- index build */
+/* Workspace bytes for gsp_index_count / gsp_index_fill on a CSR of n_docs rows. */
+int64_t gsp_index_ws_bytes(int64_t n_docs, int32_t V, int32_t block_docs);
+/* Pass 1 (replaces the argsort/bincount/cumsum of build_gpu_index_from_csr :47-58):
+ * lengths, padded, offsets and block_starts on the device; *total_padded on the host
+ * (this call synchronises the stream).  Column ids outside [0, V) -> GSP_ERR_ARG. */
+int gsp_index_count(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* indptr,
+                    const int32_t* indices, int32_t* lengths, int32_t* padded,
+                    int64_t* offsets, uint32_t* block_starts, int64_t* total_padded,
+                    void* ws, int64_t ws_bytes, void* stream);
+/* Pass 2 (replaces the fill loop :60-72): stable scatter of every CSR entry to its
+ * term's list (doc ids ascend), -1/0 padding, max_scores. */
+int gsp_index_fill(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* indptr,
+                   const int32_t* indices, const float* data, const int64_t* offsets,
+                   const int32_t* lengths, const uint32_t* block_starts, int64_t total_padded,
+                   int32_t* doc_ids, float* weights, float* max_scores, void* ws,
+                   int64_t ws_bytes, void* stream);
+/* fp32 weights -> bf16 (round to nearest even) or uint8 impacts with per-term scale
+ * max_scores[t] / 255 (q = clamp(rint(w / scale), 0, 255)). */
+int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t* offsets,
+                       const int32_t* padded, const float* max_scores, const float* weights,
+                       int32_t wdtype, void* out_weights, float* term_scale, void* stream);
+/* Counts posting lists that are not ascending in doc id (writes *n_bad on the host). */
+int gsp_check_sorted(int32_t V, const int32_t* doc_ids, const int64_t* offsets,
+                     const int32_t* lengths, int64_t* n_bad, void* stream);
+
+/* ---------------------------------------------------------------- chunk bounds */
+/* build_chunk_boundaries: out int64 [n_chunks+1, V], out[c][t] = offsets[t] + number of
+ * postings of t with doc id < min(c*doc_chunk, n_docs).  GSP_ERR_UNSORTED if any list
+ * is not ascending (the reference raises ValueError). */
+int gsp_chunk_bounds(int64_t n_docs, int32_t V, int64_t doc_chunk, const int32_t* doc_ids,
+                     const int64_t* offsets, const int32_t* lengths, int64_t* out,
+                     void* stream);
+
+/* ---------------------------------------------------------------- scoring */
+typedef struct gsp_index_view {
+    int64_t n_docs;            /* documents in this shard (local ids 0..n_docs-1) */
+    int64_t doc_base;          /* global id of local document 0 */
+    int32_t V;
+    int32_t block_docs;        /* documents per block_starts row */
+    int32_t wdtype;            /* GSP_W_* */
+    int32_t pad_;
+    const int32_t* doc_ids;
+    const void* weights;
+    const float* term_scale;   /* uint8 mode only */
+    const int64_t* offsets;
+    const int32_t* lengths;
+    const uint32_t* block_starts;
+} gsp_index_view;
+
+/* Workspace bytes for gsp_score_topk with this batch shape (a negative status on error). */
+int64_t gsp_score_ws_bytes(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k);
+/* Exact scores of B queries (qi int32 [B, W], -1 padded; ids outside [0, V) skipped;
+ * qs fp32 [B, W]) against every document, then the exact top-k per query:
+ * out_scores fp32 [B, k'] descending, out_ids int64 [B, k'] global doc ids, with
+ * k' = min(k, n_docs) and ties broken by ascending doc id.  Each document's score is
+ * the fp32 sum of fl(q_w * d_w) over the query's (term id, slot) pairs in ascending
+ * order, so results are bitwise reproducible.  Optionally also writes the packed
+ * (score key << 32 | ~doc id) top-k to out_keys [B, k'] for a later gsp_merge_topk. */
+int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const float* qs, int64_t B,
+                   int64_t W, int64_t k, float* out_scores, int64_t* out_ids,
+                   uint64_t* out_keys, void* ws, int64_t ws_bytes, void* stream);
+
+/* ---------------------------------------------------------------- selection */
+/* Merge R candidate lists per query into the exact top-k.  keys: packed uint64
+ * (fkey(score) << 32 | (0xFFFFFFFF - doc id)), list r of query b at
+ * keys + b*stride_b + r*stride_r, holding counts[r] valid entries.  Writes k' =
+ * min(k, sum(counts)) results per query (scores fp32, ids int64 and, if non-null,
+ * keys).  Replaces the host-side shard merge and the running torch.topk merge. */
+int gsp_merge_topk(const uint64_t* keys, int64_t B, int64_t R, int64_t stride_b,
+                   int64_t stride_r, const int32_t* counts_host, int64_t k,
+                   float* out_scores, int64_t* out_ids, uint64_t* out_keys, void* stream);
+/* compacted_topk: top-min(k, L) of row entries >= tau[b] of scores [B, L] (row stride
+ * `stride` floats), (score desc, column asc), padded with (-inf, 0) when fewer. */
+int64_t gsp_compacted_ws_bytes(int64_t B, int64_t L, int64_t k, int64_t max_cand);
+int gsp_compacted_topk(const float* scores, int64_t B, int64_t L, int64_t stride,
+                       const float* tau, int64_t k, int64_t max_cand, float* out_v,
+                       int64_t* out_i, void* ws, int64_t ws_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GPUSPARSE_H */

@@ -1,0 +1,377 @@
+"""CPU oracle for the exact learned-sparse scoring path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline / reference arm of
+``bench.py`` may import this module.  The product (``gpu-sparse_b200/``) never does.
+
+What is restated here (reference paths are relative to the GPUSparse checkout):
+
+* ``build_index_reference``: ``src/run_correctness_verification.py:32-84``
+  (``build_gpu_index_from_csr``) line for line in numpy: stable argsort of the COO
+  columns, ``np.unique`` counts, pad to 32, exclusive cumsum -> offsets, -1/0 fill,
+  per-term max.  ``build_index`` is the same algorithm as a C counting sort
+  (``oracle.c``) for large inputs; a test pins the two against each other.
+* ``chunk_bounds``: ``src/triton_kernel_chunked.py:83-122`` (ascending check raising
+  ``ValueError`` :96-108, per-term ``searchsorted`` :110-121).
+* ``compacted_topk``: ``src/fused_topk.py:71-103`` (keep ``score >= tau``, top-k of
+  the survivors padded with (-inf, 0), exact fallback on overflow).
+* ``score_topk`` / ``score_full``: ``src/triton_kernel.py:93-156,199`` in the
+  canonical summation order documented in ``oracle.c``.
+* ``score_dense_f64``: the exhaustive dense reference
+  (``src/remeasure_2026_09.py:238-258``) in fp64.
+* ``synth_*``: the seeded synthetic SPLADE-shaped generator (twin of the GPU one).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_SO = os.path.join(_HERE, "liboracle.so")
+BLOCK = 32
+WTAB_SEGS = 65536
+
+
+def build_lib(force: bool = False) -> str:
+    """Compile oracle.c into oracle/liboracle.so (no FMA contraction)."""
+    src = os.path.join(_HERE, "oracle.c")
+    if force or not os.path.exists(_SO) or os.path.getmtime(_SO) < os.path.getmtime(src):
+        subprocess.check_call(["gcc", "-O3", "-ffp-contract=off", "-fno-fast-math", "-fPIC",
+                               "-shared", "-pthread", src, "-o", _SO])
+    return _SO
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build_lib()
+        L = ctypes.CDLL(_SO)
+        i32, i64, u32, u64 = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_uint64
+        p = ctypes.c_void_p
+        L.orc_synth_nnz.argtypes = [u64, u32, u64, i64, i32, p, i32, i32, i32, p]
+        L.orc_synth_fill.argtypes = [u64, u32, u64, i64, i32, p, p, p, p, p, p, i32]
+        L.orc_build_lengths.argtypes = [i64, i32, p, p]
+        L.orc_build_fill.argtypes = [i64, i32, p, p, p, p, p, p, p]
+        L.orc_score_topk.argtypes = [i64, i32, p, p, p, p, i64, i64, p, p, i64, i64, i32, p, p]
+        L.orc_score_full.argtypes = [i64, i32, p, p, p, p, i64, i64, p, p, i32, p]
+        L.orc_score_dense_f64.argtypes = [i64, i32, p, p, p, i64, i64, p, p, p]
+        for f in ("orc_synth_nnz", "orc_synth_fill", "orc_build_lengths", "orc_build_fill",
+                  "orc_score_topk", "orc_score_full", "orc_score_dense_f64"):
+            getattr(L, f).restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+def nthreads_default() -> int:
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:  # pragma: no cover
+        return max(1, os.cpu_count() or 1)
+
+
+# ---------------------------------------------------------------- synthetic law tables
+
+@dataclass(frozen=True)
+class Law:
+    """One item law (documents or queries) of the synthetic SPLADE-shaped corpus."""
+    zipf_s: float = 1.1
+    nnz_mean: float = 180.0
+    nnz_sd: float = 80.0
+    nnz_lo: int = 20
+    nnz_hi: int = 600
+    w_mu: float = 0.8
+    w_sd: float = 0.7
+    min_nnz_item0: int = 0
+
+
+DOC_LAW = Law()
+QUERY_LAW = Law(nnz_mean=30.0, nnz_sd=15.0, nnz_lo=5, nnz_hi=128, min_nnz_item0=107)
+
+
+def term_cdf(V: int, s: float) -> np.ndarray:
+    """CDF over term ids of p(rank r) ~ r^-s, rank r <-> term id r-1."""
+    r = np.arange(1, V + 1, dtype=np.float64)
+    c = np.cumsum(r ** (-s))
+    c /= c[-1]
+    c[-1] = 1.0
+    return c
+
+
+def nnz_cdf(law: Law) -> np.ndarray:
+    """CDF of clip(round(LogNormal(mean, sd)), lo, hi) over n = lo..hi."""
+    s2 = math.log(1.0 + law.nnz_sd ** 2 / law.nnz_mean ** 2)
+    mu, sig = math.log(law.nnz_mean) - s2 / 2.0, math.sqrt(s2)
+    ns = np.arange(law.nnz_lo, law.nnz_hi + 1)
+    c = np.array([0.5 * (1.0 + math.erf((math.log(n + 0.5) - mu) / (sig * math.sqrt(2.0))))
+                  for n in ns], dtype=np.float64)
+    c[-1] = 1.0
+    return c
+
+
+GUIDE = 65536
+
+
+def term_guide(cdf: np.ndarray) -> np.ndarray:
+    """guide[j] = first i with cdf[i] > j / GUIDE, j = 0..GUIDE (last clamped to V-1)."""
+    g = np.searchsorted(cdf, np.arange(GUIDE + 1, dtype=np.float64) / GUIDE, side="right")
+    return np.minimum(g, len(cdf) - 1).astype(np.int32)
+
+
+def weight_table(law: Law) -> np.ndarray:
+    """Quantiles of log1p(relu(N(mu, sd))) at u = i / 65536 (last point at 1 - 2^-20)."""
+    from scipy.special import ndtri
+    u = np.arange(WTAB_SEGS + 1, dtype=np.float64) / WTAB_SEGS
+    u[-1] = 1.0 - 2.0 ** -20
+    x = law.w_mu + law.w_sd * ndtri(u)
+    return np.log1p(np.maximum(x, 0.0))
+
+
+def synth_csr(n: int, V: int = 30522, seed: int = 0, kind: int = 0, first: int = 0,
+              law: Law | None = None, nthreads: int | None = None):
+    """Items [first, first+n) of the seeded generator as (indptr i64, indices i32, data f32)."""
+    law = law or (DOC_LAW if kind == 0 else QUERY_LAW)
+    L = lib()
+    nc = nnz_cdf(law)
+    nnz = np.empty(n, dtype=np.int32)
+    rc = L.orc_synth_nnz(seed, kind, first, n, V, _p(nc), len(nc), law.nnz_lo,
+                         law.min_nnz_item0, _p(nnz))
+    assert rc == 0
+    indptr = np.zeros(n + 1, dtype=np.int64)
+    np.cumsum(nnz, out=indptr[1:])
+    indices = np.empty(int(indptr[-1]), dtype=np.int32)
+    data = np.empty(int(indptr[-1]), dtype=np.float32)
+    tc, wt = term_cdf(V, law.zipf_s), weight_table(law)
+    gd = term_guide(tc)
+    rc = L.orc_synth_fill(seed, kind, first, n, V, _p(tc), _p(gd), _p(wt), _p(indptr),
+                          _p(indices), _p(data), nthreads or nthreads_default())
+    assert rc == 0
+    return indptr, indices, data
+
+
+def synth_queries(B: int, V: int = 30522, seed: int = 0, law: Law | None = None):
+    """(qi int32 [B, W] padded with -1, qs fp32 [B, W] padded with 0), W = max nnz."""
+    indptr, indices, data = synth_csr(B, V, seed, kind=1, law=law or QUERY_LAW)
+    nnz = np.diff(indptr)
+    W = int(nnz.max()) if B else 1
+    qi = np.full((B, W), -1, dtype=np.int32)
+    qs = np.zeros((B, W), dtype=np.float32)
+    for b in range(B):
+        qi[b, :nnz[b]] = indices[indptr[b]:indptr[b + 1]]
+        qs[b, :nnz[b]] = data[indptr[b]:indptr[b + 1]]
+    return qi, qs
+
+
+# ---------------------------------------------------------------- index build
+
+@dataclass
+class Index:
+    doc_ids: np.ndarray
+    scores: np.ndarray
+    offsets: np.ndarray
+    lengths: np.ndarray
+    padded_lengths: np.ndarray
+    max_scores: np.ndarray
+    num_docs: int
+    vocab_size: int
+
+
+def build_index_reference(csr, vocab_size: int | None = None) -> Index:
+    """src/run_correctness_verification.py:32-84 restated in numpy (V from the matrix
+    width when not given; the reference hard-codes VOCAB_SIZE = 30522 at :28)."""
+    num_docs = csr.shape[0]
+    V = int(vocab_size if vocab_size is not None else csr.shape[1])
+    coo = csr.tocoo()
+    rows = coo.row.astype(np.int32)
+    cols = coo.col.astype(np.int32)
+    vals = coo.data.astype(np.float32)
+    sort_idx = np.argsort(cols, kind="stable")
+    sorted_terms, sorted_docs, sorted_scores = cols[sort_idx], rows[sort_idx], vals[sort_idx]
+    unique_terms, counts = np.unique(sorted_terms, return_counts=True)
+    lengths = np.zeros(V, dtype=np.int32)
+    lengths[unique_terms] = counts
+    padded = ((lengths + BLOCK - 1) // BLOCK) * BLOCK
+    offsets = np.zeros(V, dtype=np.int64)
+    np.cumsum(padded[:-1], out=offsets[1:])
+    total = int(offsets[-1] + padded[-1])
+    all_docs = np.full(total, -1, dtype=np.int32)
+    all_scores = np.zeros(total, dtype=np.float32)
+    max_scores = np.zeros(V, dtype=np.float32)
+    src = 0
+    for i, t in enumerate(unique_terms):
+        n = counts[i]
+        off = offsets[t]
+        all_docs[off:off + n] = sorted_docs[src:src + n]
+        all_scores[off:off + n] = sorted_scores[src:src + n]
+        max_scores[t] = sorted_scores[src:src + n].max()
+        src += n
+    return Index(all_docs, all_scores, offsets, lengths, padded.astype(np.int32), max_scores,
+                 num_docs, V)
+
+
+def build_index(indptr: np.ndarray, indices: np.ndarray, data: np.ndarray, V: int) -> Index:
+    """The same layout as build_index_reference via the C stable counting sort."""
+    L = lib()
+    N = len(indptr) - 1
+    indptr = np.ascontiguousarray(indptr, dtype=np.int64)
+    indices = np.ascontiguousarray(indices, dtype=np.int32)
+    data = np.ascontiguousarray(data, dtype=np.float32)
+    lengths = np.empty(V, dtype=np.int32)
+    assert L.orc_build_lengths(len(indices), V, _p(indices), _p(lengths)) == 0
+    padded = ((lengths + BLOCK - 1) // BLOCK) * BLOCK
+    offsets = np.zeros(V, dtype=np.int64)
+    np.cumsum(padded[:-1], out=offsets[1:])
+    total = int(offsets[-1] + padded[-1]) if V else 0
+    doc_ids = np.full(total, -1, dtype=np.int32)
+    scores = np.zeros(total, dtype=np.float32)
+    max_scores = np.zeros(V, dtype=np.float32)
+    assert L.orc_build_fill(N, V, _p(indptr), _p(indices), _p(data), _p(offsets), _p(doc_ids),
+                            _p(scores), _p(max_scores)) == 0
+    return Index(doc_ids, scores, offsets, lengths, padded.astype(np.int32), max_scores, N, V)
+
+
+def chunk_bounds(index: Index, doc_chunk: int) -> np.ndarray:
+    """src/triton_kernel_chunked.py:83-122: int64 [n_chunks+1, V] posting offsets."""
+    doc_ids, offsets = index.doc_ids, index.offsets.astype(np.int64)
+    lengths = index.lengths.astype(np.int64)
+    V, N = int(index.vocab_size), int(index.num_docs)
+    n_chunks = (N + doc_chunk - 1) // doc_chunk
+    n_bad = 0
+    for t in np.nonzero(lengths)[0]:
+        if np.any(np.diff(doc_ids[offsets[t]:offsets[t] + lengths[t]]) < 0):
+            n_bad += 1
+    if n_bad:
+        raise ValueError(f"{n_bad} posting lists are not ascending in doc_id")
+    bounds = np.zeros((n_chunks + 1, V), dtype=np.int64)
+    edges = [c * doc_chunk for c in range(n_chunks)] + [N]
+    for t in range(V):
+        L = lengths[t]
+        if L == 0:
+            bounds[:, t] = offsets[t]
+            continue
+        seg = doc_ids[offsets[t]:offsets[t] + L]
+        first = int(np.searchsorted(seg, 0, side="left"))
+        rel = np.searchsorted(seg[first:], edges, side="left")
+        bounds[:, t] = offsets[t] + first + rel
+    return bounds
+
+
+# ---------------------------------------------------------------- scoring
+
+def fkey(x: np.ndarray) -> np.ndarray:
+    """Order-preserving uint32 key of fp32 values (-0 folded onto +0)."""
+    b = (np.asarray(x, dtype=np.float32) + np.float32(0.0)).view(np.uint32)
+    return np.where(b & 0x80000000, ~b, b | 0x80000000).astype(np.uint32)
+
+
+def topk_rows(S: np.ndarray, k: int, id_base: int = 0):
+    """Exact top-k of each row of S by (score desc, index asc)."""
+    B, N = S.shape
+    k = min(k, N)
+    key = fkey(S).astype(np.uint64)
+    comp = (key << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - np.arange(N, dtype=np.uint64))[None, :]
+    idx = np.empty((B, k), dtype=np.int64)
+    for b in range(B):
+        idx[b] = np.argsort(comp[b])[::-1][:k]   # composite keys are unique
+    vals = np.take_along_axis(S, idx, axis=1)
+    return vals.astype(np.float32), idx + id_base
+
+
+def score_topk(index: Index, qi: np.ndarray, qs: np.ndarray, k: int, weights=None,
+               id_base: int = 0, nthreads: int | None = None):
+    """Exact top-k (fp32 scores [B,k], int64 ids [B,k]) in the canonical order."""
+    L = lib()
+    qi = np.ascontiguousarray(qi, dtype=np.int32)
+    qs = np.ascontiguousarray(qs, dtype=np.float32)
+    B, W = qi.shape
+    N = int(index.num_docs)
+    kk = min(k, N)
+    w = np.ascontiguousarray(index.scores if weights is None else weights, dtype=np.float32)
+    out_s = np.zeros((B, kk), dtype=np.float32)
+    out_i = np.zeros((B, kk), dtype=np.int64)
+    rc = L.orc_score_topk(N, int(index.vocab_size), _p(index.doc_ids), _p(w), _p(index.offsets),
+                          _p(index.lengths), B, W, _p(qi), _p(qs), kk, id_base,
+                          nthreads or nthreads_default(), _p(out_s), _p(out_i))
+    assert rc == 0
+    return out_s, out_i
+
+
+def score_full(index: Index, qi: np.ndarray, qs: np.ndarray, weights=None,
+               nthreads: int | None = None) -> np.ndarray:
+    """The whole fp32 [B, N] score matrix in the canonical order."""
+    L = lib()
+    qi = np.ascontiguousarray(qi, dtype=np.int32)
+    qs = np.ascontiguousarray(qs, dtype=np.float32)
+    B, W = qi.shape
+    N = int(index.num_docs)
+    w = np.ascontiguousarray(index.scores if weights is None else weights, dtype=np.float32)
+    out = np.zeros((B, N), dtype=np.float32)
+    rc = L.orc_score_full(N, int(index.vocab_size), _p(index.doc_ids), _p(w), _p(index.offsets),
+                          _p(index.lengths), B, W, _p(qi), _p(qs), nthreads or nthreads_default(),
+                          _p(out))
+    assert rc == 0
+    return out
+
+
+def score_dense_f64(indptr, indices, data, V: int, qi, qs) -> np.ndarray:
+    L = lib()
+    indptr = np.ascontiguousarray(indptr, dtype=np.int64)
+    indices = np.ascontiguousarray(indices, dtype=np.int32)
+    data = np.ascontiguousarray(data, dtype=np.float32)
+    qi = np.ascontiguousarray(qi, dtype=np.int32)
+    qs = np.ascontiguousarray(qs, dtype=np.float32)
+    B, W = qi.shape
+    N = len(indptr) - 1
+    out = np.zeros((B, N), dtype=np.float64)
+    assert L.orc_score_dense_f64(N, V, _p(indptr), _p(indices), _p(data), B, W, _p(qi), _p(qs),
+                                 _p(out)) == 0
+    return out
+
+
+def compacted_topk(scores: np.ndarray, tau: np.ndarray, k: int):
+    """src/fused_topk.py:71-103 semantics: top-min(k, L) of the entries >= tau per row,
+    padded with (-inf, 0) when fewer survive; ties by ascending column."""
+    B, L = scores.shape
+    kk = min(k, L)
+    v = np.full((B, kk), -np.inf, dtype=np.float32)
+    ix = np.zeros((B, kk), dtype=np.int64)
+    for b in range(B):
+        keep = np.nonzero(scores[b] >= tau[b])[0]
+        if len(keep) == 0:
+            continue
+        sv, si = topk_rows(scores[b:b + 1, keep], kk)
+        n = sv.shape[1]
+        v[b, :n] = sv[0]
+        ix[b, :n] = keep[si[0]]
+    return v, ix
+
+
+def dequantize_u8(q: np.ndarray, scale: np.ndarray, offsets, lengths, padded) -> np.ndarray:
+    """fp32 weights q * scale_t of a uint8 posting array (one fp32 rounding)."""
+    term_of = np.repeat(np.arange(len(padded)), padded)
+    return (q.astype(np.float32) * scale[term_of].astype(np.float32)).astype(np.float32)
+
+
+def quantize_u8(index: Index):
+    """uint8 impacts with per-term fp32 scale max_t / 255, round-to-nearest (ties to
+    even), the config-3 weight law; returns (q uint8 [P_pad], scale fp32 [V])."""
+    V = index.vocab_size
+    scale = (index.max_scores.astype(np.float32) / np.float32(255.0)).astype(np.float32)
+    scale[index.lengths == 0] = 0.0
+    term_of = np.repeat(np.arange(V), index.padded_lengths)
+    st = scale[term_of]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        r = np.where(st > 0, index.scores / st, 0.0).astype(np.float32)
+    q = np.clip(np.rint(r), 0, 255).astype(np.uint8)
+    return q, scale

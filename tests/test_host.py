@@ -1,0 +1,119 @@
+"""Host-side logic that needs no GPU: the C ABI library loads and exports every declared
+symbol, reference argument validation, plug-in helpers, shard layout, key decoding and
+the synthetic generator's law."""
+import json
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLD = os.path.join(ROOT, "tests", "golden")
+
+
+def header_symbols():
+    txt = open(os.path.join(ROOT, "include", "gpusparse.h")).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(gsp_[a-z0-9_]+)\s*\(", txt)))
+
+
+def test_library_exports_every_declared_symbol():
+    import gpusparse._lib as L
+    lib = L.lib()
+    syms = header_symbols()
+    assert syms, "no declarations parsed"
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert set(syms) == set(L.EXPORTS)
+    assert lib.gsp_version() == 1
+
+
+def test_no_cpu_fallback():
+    import gpusparse
+    with pytest.raises(RuntimeError):
+        gpusparse.build_from_csr_tensors(torch.zeros(2, dtype=torch.int64),
+                                         torch.zeros(0, dtype=torch.int32),
+                                         torch.zeros(0), 10, device="cpu")
+
+
+@pytest.mark.parametrize("bad", [0, -4, 3, 96])
+def test_block_pl_must_be_power_of_two(bad):
+    import gpusparse
+    with pytest.raises(AssertionError):
+        gpusparse.triton_fused_score(None, None, None, top_k=10, block_pl=bad)
+    with pytest.raises(AssertionError):
+        gpusparse.triton_chunked_score(None, None, None, block_pl=bad)
+    with pytest.raises(AssertionError):
+        gpusparse.triton_chunked_score_fused(None, None, None, block_pl=bad)
+
+
+def test_plugin_helpers_match_reference():
+    meta = json.load(open(os.path.join(GOLD, "reference_meta.json")))["plugin"]
+    from lsr_benchmark_engine import gpusparse_retrieval as P
+    d_emb = [tuple(x) for x in meta["d_emb"]]
+    q_emb = [tuple(x) for x in meta["q_emb"]]
+    dim = P.determine_dimension(d_emb, q_emb)
+    assert dim == meta["dim"]
+    qids, qcsr = P.to_csr(q_emb, dim)
+    ti, ts, mx = P.to_query_tensors(qcsr, "cpu")
+    assert mx == meta["max_nnz"]
+    assert ti.tolist() == meta["ti"] and ts.tolist() == meta["ts"]
+
+
+def test_shard_layout_and_counts():
+    from gpusparse.distributed import ShardLayout
+    for N, G in [(10, 3), (8_800_000, 8), (5, 8)]:
+        sizes = ShardLayout(N, G, 0).sizes()
+        assert sum(sizes) == N and max(sizes) - min(sizes) <= 1
+        lo = [ShardLayout(N, G, r).lo for r in range(G)]
+        assert lo == sorted(lo) and lo[0] == 0
+        assert ShardLayout(N, G, G - 1).hi == N
+    lay = ShardLayout(5, 8, 0)
+    assert lay.sizes() == [0, 1, 0, 1, 1, 0, 1, 1]
+    assert lay.list_counts(3) == [0, 1, 0, 1, 1, 0, 1, 1]
+    assert ShardLayout(100, 2, 1).list_counts(30) == [30, 30]
+
+
+def test_key_packing_orders_like_reference_ranking():
+    from gpusparse.distributed import decode_keys
+    rng = np.random.default_rng(3)
+    s = rng.standard_normal(500).astype(np.float32)
+    s[::7] = 0.0
+    s[1::11] = s[0]
+    d = rng.permutation(500).astype(np.uint64)
+    keys = (O.fkey(s).astype(np.uint64) << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - d)
+    order = np.argsort(keys)[::-1]
+    ref = np.lexsort((d, -s.astype(np.float64)))
+    assert np.array_equal(order, ref)
+    ds, di = decode_keys(torch.from_numpy(keys.view(np.int64)))
+    assert np.array_equal(ds.numpy(), s) and np.array_equal(di.numpy(), d.astype(np.int64))
+
+
+def test_generator_law_and_range_independence():
+    ip, ix, dt = O.synth_csr(4000, seed=11)
+    nnz = np.diff(ip)
+    assert 20 <= nnz.min() and nnz.max() <= 600 and 170 < nnz.mean() < 190
+    assert 0.11 < (dt == 0).mean() < 0.14                  # P(N(0.8,0.7) < 0) = 0.1265
+    for r in range(0, 4000, 997):                          # distinct terms per document
+        row = ix[ip[r]:ip[r + 1]]
+        assert len(np.unique(row)) == len(row)
+    a = O.synth_csr(1500, seed=11, first=2500)             # any item range on its own
+    assert np.array_equal(a[1], ix[ip[2500]:]) and np.array_equal(a[2], dt[ip[2500]:])
+    qi, qs = O.synth_queries(300, seed=2)
+    n = (qi >= 0).sum(1)
+    assert n[0] >= 107 and 5 <= n.min() and n.max() <= 128 and 25 < n.mean() < 35
+
+
+def test_oracle_quantisation_roundtrip():
+    ip, ix, dt = O.synth_csr(500, seed=4)
+    idx = O.build_index(ip, ix, dt, 30522)
+    q, scale = O.quantize_u8(idx)
+    w = O.dequantize_u8(q, scale, idx.offsets, idx.lengths, idx.padded_lengths)
+    real = idx.doc_ids >= 0
+    err = np.abs(w[real] - idx.scores[real])
+    term_of = np.repeat(np.arange(30522), idx.padded_lengths)[real]
+    assert np.all(err <= scale[term_of] * 0.5 + 1e-7)
