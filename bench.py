@@ -1,0 +1,440 @@
+#!/usr/bin/env python3
+"""Benchmark of the exact learned-sparse scoring path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1: doc-range shards)
+
+A step scores one batch of queries against the whole corpus and returns the exact top-k
+(k = 1000) per query.  The corpus is a BASELINE config (default 2: 8.8M documents,
+batch 1000) generated on each GPU from the seeded synthetic SPLADE-shaped law; with N
+GPUs every rank builds the index of its own contiguous doc range and the per-shard top-k
+lists are merged after one NCCL all-gather.  Work per step is fixed as N grows (strong
+scaling).
+
+Reported:
+* value / ms_per_step / p50: device time (CUDA events, max over ranks) of K steps with
+  queries and index resident in HBM (index >> L2, so no flush is needed between steps);
+* e2e: the same steps through the public API with the query batch copied from pinned host
+  memory and the top-k copied back every step;
+* roofline: the scoring kernel's own launches timed with CUDA events on its stream;
+  achieved = algorithmic bytes per launch / mean launch time, against the measured HBM
+  copy bandwidth (MEASURED_PEAKS.json);
+* cpu_baseline (rank 0, N = 1): the CPU oracle (a C restatement of the reference's
+  scatter-add + top-k) on a bounded sample of the same workload, all host threads.
+
+--impl reference times the reference's CPU path for this workload (the same C oracle
+port, since the reference itself is Python/Triton and only its CPU restatement runs on
+the GPU box): rank 0 only, the others exit immediately.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import resource
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "gpu-sparse_b200")]
+
+METRIC = ("queries/sec & batch p50 latency at k=1000; scorer HBM GB/s vs peak "
+          "(1/2/4/8 B200)")
+V = 30522
+CONFIGS = {
+    0: dict(num_docs=100_000, batch=500, zipf_s=1.1, wdtype="fp32"),
+    1: dict(num_docs=1_000_000, batch=1000, zipf_s=1.1, wdtype="fp32"),
+    2: dict(num_docs=8_800_000, batch=1000, zipf_s=1.1, wdtype="fp32"),
+    3: dict(num_docs=8_800_000, batch=1000, zipf_s=1.1, wdtype="u8"),
+    4: dict(num_docs=50_000_000, batch=4096, zipf_s=1.2, wdtype="fp32"),
+}
+WBYTES = {"fp32": 4, "bf16": 2, "u8": 1}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--num-docs", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--k", type=int, default=1000)
+    ap.add_argument("--wdtype", choices=["fp32", "bf16", "u8"], default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="target CPU work of the bounded CPU-baseline sample")
+    return ap.parse_args()
+
+
+def workload(args):
+    c = dict(CONFIGS[args.config])
+    if args.num_docs:
+        c["num_docs"] = args.num_docs
+    if args.batch:
+        c["batch"] = args.batch
+    if args.wdtype:
+        c["wdtype"] = args.wdtype
+    c["k"] = min(args.k, c["num_docs"])
+    c["name"] = (f"config{args.config}: {c['num_docs']:,} docs, batch {c['batch']}, "
+                 f"k={c['k']}, V={V}, zipf {c['zipf_s']}, {c['wdtype']} weights")
+    return c
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self, gpus):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.flush()
+        self.f.seek(0)
+        sm, mx, reasons = [], [], set()
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        idxs = ([int(x) for x in vis.split(",") if x.strip().isdigit()] if vis else
+                list(range(gpus)))[:gpus]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in idxs:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.f.name)
+        if not sm:
+            return None
+        load = [x for x in sm if x > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def bytes_alg(index, qi, B, k, wdtype):
+    """Algorithmic bytes of one scoring launch: the postings of the batch's unique terms
+    (doc id + weight), one fp32 accumulator write + read per (query, document), and the
+    top-k output."""
+    import torch
+    t = qi[(qi >= 0) & (qi < index.vocab_size)].long().unique()
+    post = int(index.lengths[t].long().sum().item())
+    b = post * (4 + WBYTES[wdtype]) + 2 * 4 * B * int(index.num_docs) + 8 * B * k
+    if wdtype == "u8":
+        b += 4 * int(t.numel())
+    return b, post
+
+
+def cpu_sample(index, qi, qs, k, gpu_s, gpu_i, target_s):
+    """The CPU oracle on a bounded sample of queries of the same workload (all host
+    threads), plus a bit-exact parity check of those queries against the GPU result."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    import gpusparse
+    nt = O.nthreads_default()
+    oidx = O.Index(index.doc_ids.cpu().numpy(), None, index.offsets.cpu().numpy(),
+                   index.lengths.cpu().numpy(), index.padded_lengths.cpu().numpy(), None,
+                   int(index.num_docs), int(index.vocab_size))
+    w = gpusparse.dequantized_weights(index).cpu().numpy()
+    qi_h, qs_h = qi.cpu().numpy(), qs.cpu().numpy()
+    B = qi_h.shape[0]
+    # calibrate on one query per thread, then size the timed sample to ~target_s
+    nq = min(B, nt)
+    t0 = time.perf_counter()
+    O.score_topk(oidx, qi_h[:nq], qs_h[:nq], k, weights=w, nthreads=nt)
+    dt = time.perf_counter() - t0
+    reps = max(1, int(target_s / max(dt, 1e-3)))
+    nq = min(B, nq * reps)
+    r0 = resource.getrusage(resource.RUSAGE_SELF)
+    t0 = time.perf_counter()
+    s, i = O.score_topk(oidx, qi_h[:nq], qs_h[:nq], k, weights=w, nthreads=nt)
+    wall = time.perf_counter() - t0
+    r1 = resource.getrusage(resource.RUSAGE_SELF)
+    cpu = (r1.ru_utime - r0.ru_utime) + (r1.ru_stime - r0.ru_stime)
+    exact = bool(np.array_equal(s, gpu_s[:nq]) and np.array_equal(i, gpu_i[:nq]))
+    return {"value": nq / wall, "unit": "queries/s", "cores": nt, "kind": "port",
+            "sample": f"{nq} of the {B} queries against all {int(index.num_docs):,} docs",
+            "wall_s": round(wall, 3), "cpu_s": round(cpu, 3),
+            "cpu_over_wall": round(cpu / wall, 2), "parity_bit_exact_vs_gpu": exact}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import gpusparse
+    from gpusparse import _lib as L
+    from gpusparse import synth
+    from gpusparse.distributed import ShardLayout, sharded_score_topk
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
+    wl = workload(args)
+    N, B, k, wd = wl["num_docs"], wl["batch"], wl["k"], wl["wdtype"]
+    lay = ShardLayout(N, world, rank)
+    dlaw = synth.Law(zipf_s=wl["zipf_s"])
+    qlaw = synth.Law(zipf_s=wl["zipf_s"], nnz_mean=30.0, nnz_sd=15.0, nnz_lo=5, nnz_hi=128,
+                     min_nnz_item0=107)
+    t0 = time.time()
+    index = synth.synth_index(N, V, seed=0, law=dlaw, doc_range=(lay.lo, lay.hi), device=dev,
+                              weight_dtype=wd, keep_fp32=(wd == "fp32"))
+    qi, qs = synth.synth_queries(B, V, seed=1, law=qlaw, device=dev)
+    torch.cuda.synchronize()
+    build_s = time.time() - t0
+
+    def step(qi_d, qs_d):
+        return sharded_score_topk(index, lay, qi_d, qs_d, k)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 0)):
+        out = step(qi, qs)
+    torch.cuda.synchronize()
+    barrier()
+
+    # ---- device-timed steps (inputs resident)
+    clocks = ClockSampler()
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.3)
+    L.check(L.lib().gsp_profile_enable(1), "profile")
+    K = args.steps
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(K + 1)]
+    barrier()
+    torch.cuda.synchronize()
+    ev[0].record()
+    for s_ in range(K):
+        out = step(qi, qs)
+        ev[s_ + 1].record()
+    torch.cuda.synchronize()
+    barrier()
+    per_step = [ev[j].elapsed_time(ev[j + 1]) for j in range(K)]
+    total_ms = max_over_ranks(ev[0].elapsed_time(ev[K]))
+    import ctypes
+    tot, n = ctypes.c_double(0.0), ctypes.c_int64(0)
+    L.check(L.lib().gsp_profile_collect(ctypes.byref(tot), ctypes.byref(n)), "profile")
+    L.check(L.lib().gsp_profile_enable(0), "profile")
+    kern_ms = max_over_ranks(tot.value / max(n.value, 1))
+    p50 = statistics.median(per_step)
+    p90 = sorted(per_step)[min(K - 1, int(0.9 * K))]
+    p50 = max_over_ranks(p50)
+    p90 = max_over_ranks(p90)
+    clk = clocks.stop(world) if rank == 0 else None
+
+    # ---- end to end through the public API (pinned host buffers both ways)
+    qi_h = qi.cpu().pin_memory()
+    qs_h = qs.cpu().pin_memory()
+    qi_d = torch.empty_like(qi)
+    qs_d = torch.empty_like(qs)
+    s0, i0 = out
+    s_h = torch.empty(s0.shape, dtype=s0.dtype).pin_memory()
+    i_h = torch.empty(i0.shape, dtype=i0.dtype).pin_memory()
+
+    def e2e_step():
+        qi_d.copy_(qi_h, non_blocking=True)
+        qs_d.copy_(qs_h, non_blocking=True)
+        s, i = step(qi_d, qs_d)
+        if rank == 0:
+            s_h.copy_(s, non_blocking=True)
+            i_h.copy_(i, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return s_h, i_h
+
+    for _ in range(max(args.warmup, 1)):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    h2d = qi.numel() * qi.element_size() + qs.numel() * qs.element_size()
+    d2h = s0.numel() * s0.element_size() + i0.numel() * i0.element_size()
+
+    # ---- roofline of the scoring kernel (this rank's shard)
+    balg, post = bytes_alg(index, qi, B, min(k, index.num_docs), wd)
+    balg = max_over_ranks(balg)
+    peak, peak_src = peaks()
+    achieved = balg / (kern_ms * 1e-3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "score_kernel_traffic.json")
+    if os.path.exists(tp):
+        try:
+            tj = json.load(open(tp))
+            ent = tj.get(f"config{args.config}_gpus{world}")
+            if ent:
+                traffic = ent["dram_bytes_per_launch"]
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gs, gi = (x.cpu().numpy() for x in out)
+        cpu = cpu_sample(index, qi, qs, k, gs, gi, args.cpu_seconds)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    launches_per_step = 3 if world == 1 else 4   # plan, score, shard merge (+ global merge)
+    line = {
+        "metric": METRIC,
+        "value": B * K / (total_ms * 1e-3),
+        "unit": "queries/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": total_ms / K,
+        "p50_ms": p50,
+        "p90_ms": p90,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded SPLADE-shaped law of BASELINE.json; generated on device)",
+        "config": {"workload": wl["name"], "num_docs": N, "batch": B, "k": k, "vocab": V,
+                   "weights": wd, "parallelism": f"doc-range shards x{world}" +
+                   (" + NCCL all-gather merge" if world > 1 else ""),
+                   "l2": "inputs larger than L2 (index >> 126 MB); no flush",
+                   "index_build_s": round(build_s, 2)},
+        "gpu_launches": launches_per_step * K,
+        "e2e": {"value": B * K / (e2e_ms * 1e-3), "unit": "queries/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
+                     "kernel": "score_kernel", "kernel_ms": kern_ms,
+                     "bytes_alg_per_launch": balg, "postings_per_launch": post},
+        "cpu_baseline": cpu,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args):
+    """The reference's CPU scoring path for the same workload (C oracle port)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import oracle as O
+    wl = workload(args)
+    N, B, k, wd = wl["num_docs"], wl["batch"], wl["k"], wl["wdtype"]
+    nt = O.nthreads_default()
+    dlaw = O.Law(zipf_s=wl["zipf_s"])
+    qlaw = O.Law(zipf_s=wl["zipf_s"], nnz_mean=30.0, nnz_sd=15.0, nnz_lo=5, nnz_hi=128,
+                 min_nnz_item0=107)
+    t0 = time.time()
+    ip, ix, dt = O.synth_csr(N, V, seed=0, law=dlaw, nthreads=nt)
+    idx = O.build_index(ip, ix, dt, V)
+    del ip, ix, dt
+    w = None
+    if wd == "u8":
+        q, sc = O.quantize_u8(idx)
+        w = O.dequantize_u8(q, sc, idx.offsets, idx.lengths, idx.padded_lengths)
+    elif wd == "bf16":
+        import torch
+        w = torch.from_numpy(idx.scores).bfloat16().float().numpy()
+    qi, qs = O.synth_queries(B, V, seed=1, law=qlaw)
+    build_s = time.time() - t0
+    # one step = a bounded sample of the batch sized to ~cpu-seconds, all host threads
+    t0 = time.perf_counter()
+    O.score_topk(idx, qi[:nt], qs[:nt], k, weights=w, nthreads=nt)
+    one = time.perf_counter() - t0
+    nq = int(min(B, max(nt, nt * int(max(1.0, args.cpu_seconds / 4) / max(one, 1e-3)))))
+    times, cpu = [], 0.0
+    for s_ in range(args.warmup + args.steps):
+        lo = (s_ * nq) % B
+        sel = np.arange(lo, lo + nq) % B
+        r0 = resource.getrusage(resource.RUSAGE_SELF)
+        t0 = time.perf_counter()
+        O.score_topk(idx, qi[sel], qs[sel], k, weights=w, nthreads=nt)
+        t1 = time.perf_counter()
+        r1 = resource.getrusage(resource.RUSAGE_SELF)
+        if s_ >= args.warmup:
+            times.append(t1 - t0)
+            cpu += (r1.ru_utime - r0.ru_utime) + (r1.ru_stime - r0.ru_stime)
+    wall = sum(times)
+    value = nq * len(times) / wall
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "queries/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * wall / len(times), "p50_ms": 1e3 * statistics.median(times),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded SPLADE-shaped law of BASELINE.json; generated on host)",
+        "config": {"workload": wl["name"], "num_docs": N, "batch": B, "k": k, "vocab": V,
+                   "weights": wd, "step_sample_queries": nq,
+                   "index_build_s": round(build_s, 1)},
+        "cpu_baseline": {"value": value, "unit": "queries/s", "cores": nt, "kind": "port",
+                         "sample": f"{nq} queries per step against all {N:,} docs",
+                         "cpu_over_wall": round(cpu / max(wall, 1e-9), 2)},
+        "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -25,7 +25,7 @@ import torch
 from . import _lib as L
 
 BLOCK_SIZE = 32          # posting lists are padded to a warp (src/gpu_inverted_index.py:18)
-BLOCK_DOCS = 4096        # documents per block_starts row
+BLOCK_DOCS = 1024        # documents per block_starts row = the scorer's document tile
 VOCAB_SIZE = 30522       # src/run_correctness_verification.py:28
 
 

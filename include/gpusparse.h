@@ -135,6 +135,13 @@ int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const float* qs,
                    int64_t W, int64_t k, float* out_scores, int64_t* out_ids,
                    uint64_t* out_keys, void* ws, int64_t ws_bytes, void* stream);
 
+/* Timing of the scoring kernel itself (no reference counterpart; used by the benchmark
+ * for its roofline figure): while enabled, every gsp_score_topk brackets its main kernel
+ * launch with CUDA events on the caller's stream; collect synchronises on them and returns
+ * the summed duration and the number of launches, then resets.  One device per process. */
+int gsp_profile_enable(int on);
+int gsp_profile_collect(double* total_ms, int64_t* launches);
+
 /* ---------------------------------------------------------------- selection */
 /* Merge R candidate lists per query into the exact top-k.  keys: packed uint64
  * (fkey(score) << 32 | (0xFFFFFFFF - doc id)), list r of query b at
