@@ -445,6 +445,21 @@ int warp_bytes(int qpw, int tile) { return WarpLayout(qpw, tile).total; }
 static const int kShapes[][2] = {{2, 1024}, {4, 1024}, {1, 1024}, {2, 2048}, {1, 2048}, {1, 4096},
                                  {4, 512},  {2, 512},  {4, 256}};
 
+// Workspace layout of one call for the configured shape and range count.
+void set_layout(Cfg& c, int64_t B) {
+  int64_t o = 0;
+  c.off_run_term = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 4);
+  c.off_run_b32 = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 4);
+  c.off_run_end = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 2);
+  c.off_ent_q = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 1);
+  c.off_ent_w = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 4);
+  c.off_nruns = o; o = align256(o + int64_t(c.n_slots) * 4);
+  c.off_cand = o; o = align256(o + B * int64_t(c.R) * c.C * 8);
+  c.off_cnt = o; o = align256(o + B * int64_t(c.R) * 4);
+  c.off_counter = o; o = align256(o + 4);
+  c.total = o;
+}
+
 int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) {
   GSP_REQUIRE(ix && ix->V > 0 && ix->n_docs >= 0 && ix->block_docs > 0, GSP_ERR_ARG,
               "score: bad index view");
@@ -496,17 +511,7 @@ int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) 
   c.grid = int(std::min<int64_t>(int64_t(sms) * c.ctas_per_sm,
                                  (int64_t(c.n_slots) * c.R + kWarps - 1) / kWarps));
   c.C = int(((std::max<int64_t>(2 * c.kk, c.kk + 256) + 31) / 32) * 32);
-  int64_t o = 0;
-  c.off_run_term = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 4);
-  c.off_run_b32 = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 4);
-  c.off_run_end = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 2);
-  c.off_ent_q = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 1);
-  c.off_ent_w = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 4);
-  c.off_nruns = o; o = align256(o + int64_t(c.n_slots) * 4);
-  c.off_cand = o; o = align256(o + B * int64_t(c.R) * c.C * 8);
-  c.off_cnt = o; o = align256(o + B * int64_t(c.R) * 4);
-  c.off_counter = o; o = align256(o + 4);
-  c.total = o;
+  set_layout(c, B);
   return GSP_OK;
 }
 
@@ -572,14 +577,11 @@ extern "C" int64_t gsp_score_ws_bytes(const gsp_index_view* ix, int64_t B, int64
   return c.total;
 }
 
-extern "C" int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const float* qs, int64_t B,
-                              int64_t W, int64_t k, float* out_scores, int64_t* out_ids,
-                              uint64_t* out_keys, void* ws, int64_t ws_bytes, void* stream) {
-  Cfg c;
-  int rc = make_cfg(ix, B, W, k, c);
-  if (rc) return rc;
-  GSP_REQUIRE(ws && ws_bytes >= c.total, GSP_ERR_ARG, "gsp_score_topk: workspace too small (%lld < %lld)",
-              (long long)ws_bytes, (long long)c.total);
+// Everything after the configuration: plan, scoring kernel, merge, with the workspace at ws.
+static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const float* qs, int64_t B,
+                          int64_t W, const Cfg& c, float* out_scores, int64_t* out_ids,
+                          uint64_t* out_keys, void* ws, cudaStream_t st) {
+  int rc = GSP_OK;
   GSP_REQUIRE(ix->doc_ids && ix->weights && ix->offsets && ix->lengths && ix->block_starts &&
                   (ix->wdtype != GSP_W_U8 || ix->term_scale),
               GSP_ERR_ARG, "gsp_score_topk: null index array");
@@ -587,7 +589,6 @@ extern "C" int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const
               "gsp_score_topk: global doc ids must stay below 2^32 - 1");
   if (B == 0 || c.kk == 0) return GSP_OK;
   GSP_REQUIRE(qi && qs && out_scores && out_ids, GSP_ERR_ARG, "gsp_score_topk: null argument");
-  cudaStream_t st = as_stream(stream);
   char* w = static_cast<char*>(ws);
   ScoreParams p;
   p.doc_ids = ix->doc_ids;
@@ -663,4 +664,81 @@ extern "C" int gsp_profile_collect(double* total_ms, int64_t* launches) {
   *launches = int64_t(pr.used);
   pr.used = 0;
   return GSP_OK;
+}
+
+extern "C" int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const float* qs, int64_t B,
+                              int64_t W, int64_t k, float* out_scores, int64_t* out_ids,
+                              uint64_t* out_keys, void* ws, int64_t ws_bytes, void* stream) {
+  Cfg c;
+  int rc = make_cfg(ix, B, W, k, c);
+  if (rc) return rc;
+  GSP_REQUIRE(ws && ws_bytes >= c.total, GSP_ERR_ARG, "gsp_score_topk: workspace too small (%lld < %lld)",
+              (long long)ws_bytes, (long long)c.total);
+  return score_with_cfg(ix, qi, qs, B, W, c, out_scores, out_ids, out_keys, ws, as_stream(stream));
+}
+
+// ---------------------------------------------------------------------------------------
+// Scoring without any device allocation.
+//
+// Some callers cannot allocate device memory while they serve a batch: a serving loop
+// where a cudaMalloc would synchronise the device and stall every other stream, or a host
+// application (for example a search engine that loads this library as a native plug-in
+// through a C FFI) that hands the library only its input and output buffers and owns no
+// device allocator to lend it a workspace.  gsp_score_topk_noalloc serves them: its
+// scratch (query plan, candidate buffers, work counter) lives in the file-scope array
+// below, which the CUDA runtime places on every GPU that loads this library and keeps
+// until the process exits.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;   // 32 MiB per GPU
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[256] = {nullptr};   // device address of the array, per device ordinal
+}  // namespace
+
+// Host code may not use g_noalloc_scratch as an address (it is a host-side stand-in), so
+// the device address is looked up once per device, with that device current.
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  GSP_CUDA(cudaGetDevice(&dev));
+  GSP_REQUIRE(dev >= 0 && dev < 256, GSP_ERR_UNSUPPORTED, "noalloc: device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("gsp_score_topk_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return GSP_ERR_CUDA;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return GSP_OK;
+}
+
+extern "C" int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* qi, const float* qs,
+                                      int64_t B, int64_t W, int64_t k, float* out_scores,
+                                      int64_t* out_ids, uint64_t* out_keys, void* stream) {
+  Cfg c;
+  int rc = make_cfg(ix, B, W, k, c);
+  if (rc) return rc;
+  // fewer document ranges shrink the candidate buffers; the result does not depend on
+  // the range count, only the parallelism does
+  while (c.total > int64_t(kNoAllocScratchBytes) && c.R > 1) {
+    c.R = std::max(1, c.R / 2);
+    set_layout(c, B);
+  }
+  GSP_REQUIRE(c.total <= int64_t(kNoAllocScratchBytes), GSP_ERR_UNSUPPORTED,
+              "gsp_score_topk_noalloc: this batch needs %lld bytes of scratch, more than the "
+              "fixed %lld (lower the batch size or top_k, or use gsp_score_topk with a workspace)",
+              (long long)c.total, (long long)kNoAllocScratchBytes);
+  c.grid = int(std::min<int64_t>(int64_t(num_sms()) * c.ctas_per_sm,
+                                 (int64_t(c.n_slots) * c.R + kWarps - 1) / kWarps));
+  void* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // Every buffer in the scratch is written before it is read within a call except the
+  // work counter, which score_with_cfg clears on the stream; the array keeps the previous
+  // call's contents otherwise.
+  return score_with_cfg(ix, qi, qs, B, W, c, out_scores, out_ids, out_keys, scratch, as_stream(stream));
 }

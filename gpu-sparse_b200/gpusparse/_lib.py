@@ -31,7 +31,7 @@ EXPORTS = (
     "gsp_last_error", "gsp_version", "gsp_scan_i32", "gsp_scan_ws_bytes", "gsp_synth_nnz",
     "gsp_synth_fill", "gsp_index_ws_bytes", "gsp_index_count", "gsp_index_fill",
     "gsp_index_quantize", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
-    "gsp_score_topk", "gsp_profile_enable", "gsp_profile_collect", "gsp_merge_topk",
+    "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_profile_enable", "gsp_profile_collect", "gsp_merge_topk",
     "gsp_compacted_ws_bytes", "gsp_compacted_topk",
 )
 
@@ -87,6 +87,8 @@ def lib() -> ctypes.CDLL:
             "gsp_score_ws_bytes": (i64, [ctypes.POINTER(IndexView), i64, i64, i64]),
             "gsp_score_topk": (ctypes.c_int, [ctypes.POINTER(IndexView), p, p, i64, i64, i64, p,
                                               p, p, p, i64, p]),
+            "gsp_score_topk_noalloc": (ctypes.c_int, [ctypes.POINTER(IndexView), p, p, i64, i64,
+                                                      i64, p, p, p, p]),
             "gsp_profile_enable": (ctypes.c_int, [ctypes.c_int]),
             "gsp_profile_collect": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double),
                                                    ctypes.POINTER(i64)]),

@@ -135,6 +135,20 @@ int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const float* qs,
                    int64_t W, int64_t k, float* out_scores, int64_t* out_ids,
                    uint64_t* out_keys, void* ws, int64_t ws_bytes, void* stream);
 
+/* gsp_score_topk without any device allocation, for callers that cannot allocate device
+ * memory on the call path (a serving loop where cudaMalloc would synchronise the device,
+ * or a host that gives the library only its input and output buffers).  No counterpart in
+ * the reference.  Scratch is a fixed 32 MiB array compiled into the library, placed on
+ * every GPU that loads it and held until exit; a batch whose plan and candidate buffers do
+ * not fit (about B * k * 16 bytes plus the plan) is rejected with GSP_ERR_UNSUPPORTED.
+ * Results equal gsp_score_topk's.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  All calls on a device share the one array: calls that
+ * overlap on the GPU (different streams, or threads) race and must be serialised. */
+int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* qi, const float* qs,
+                           int64_t B, int64_t W, int64_t k, float* out_scores, int64_t* out_ids,
+                           uint64_t* out_keys, void* stream);
+
 /* Timing of the scoring kernel itself (no reference counterpart; used by the benchmark
  * for its roofline figure): while enabled, every gsp_score_topk brackets its main kernel
  * launch with CUDA events on the caller's stream; collect synchronises on them and returns
