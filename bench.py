@@ -173,17 +173,18 @@ def cpu_sample(index, qi, qs, k, gpu_s, gpu_i, target_s):
                    int(index.num_docs), int(index.vocab_size))
     w = gpusparse.dequantized_weights(index).cpu().numpy()
     qi_h, qs_h = qi.cpu().numpy(), qs.cpu().numpy()
+    head = index.head_ids.cpu().numpy()
     B = qi_h.shape[0]
     # calibrate on one query per thread, then size the timed sample to ~target_s
     nq = min(B, nt)
     t0 = time.perf_counter()
-    O.score_topk(oidx, qi_h[:nq], qs_h[:nq], k, weights=w, nthreads=nt)
+    O.score_topk(oidx, qi_h[:nq], qs_h[:nq], k, weights=w, nthreads=nt, head=head)
     dt = time.perf_counter() - t0
     reps = max(1, int(target_s / max(dt, 1e-3)))
     nq = min(B, nq * reps)
     r0 = resource.getrusage(resource.RUSAGE_SELF)
     t0 = time.perf_counter()
-    s, i = O.score_topk(oidx, qi_h[:nq], qs_h[:nq], k, weights=w, nthreads=nt)
+    s, i = O.score_topk(oidx, qi_h[:nq], qs_h[:nq], k, weights=w, nthreads=nt, head=head)
     wall = time.perf_counter() - t0
     r1 = resource.getrusage(resource.RUSAGE_SELF)
     cpu = (r1.ru_utime - r0.ru_utime) + (r1.ru_stime - r0.ru_stime)
@@ -220,6 +221,10 @@ def run_ours(args):
     t0 = time.time()
     index = synth.synth_index(N, V, seed=0, law=dlaw, doc_range=(lay.lo, lay.hi), device=dev,
                               weight_dtype=wd, keep_fp32=(wd == "fp32"))
+    if world > 1:
+        from gpusparse.distributed import global_head
+        from gpusparse.index import N_HEAD, ensure_head
+        ensure_head(index, head_ids=global_head(index, N_HEAD))
     qi, qs = synth.synth_queries(B, V, seed=1, law=qlaw, device=dev)
     torch.cuda.synchronize()
     build_s = time.time() - t0
@@ -331,7 +336,7 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
-    launches_per_step = 3 if world == 1 else 4   # plan, score, shard merge (+ global merge)
+    launches_per_step = 4 if world == 1 else 5   # plan, streams, score, shard merge (+ global merge)
     line = {
         "metric": METRIC,
         "value": B * K / (total_ms * 1e-3),

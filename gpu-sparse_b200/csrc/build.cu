@@ -191,6 +191,25 @@ __global__ void chunk_bounds_kernel(int64_t n_docs, int32_t V, int64_t chunk, in
   }
 }
 
+// Dense rows of the head terms: row h holds term head_ids[h]'s weight for every document
+// (0 where the term is absent).  One warp per head term scatters its postings.
+template <typename WT>
+__global__ void head_rows_kernel(int32_t H, const int32_t* __restrict__ head_ids,
+                                 const int64_t* __restrict__ offsets, const int32_t* __restrict__ lengths,
+                                 const int32_t* __restrict__ doc_ids, const WT* __restrict__ weights,
+                                 int64_t ld, WT* __restrict__ rows) {
+  const int32_t h = blockIdx.x;
+  if (h >= H) return;
+  const int32_t t = head_ids[h];
+  const int64_t o = offsets[t];
+  const int32_t L = lengths[t];
+  WT* __restrict__ row = rows + int64_t(h) * ld;
+  for (int32_t i = threadIdx.x; i < L; i += blockDim.x) {
+    const int32_t d = doc_ids[o + i];
+    if (d >= 0 && d < ld) row[d] = weights[o + i];
+  }
+}
+
 int64_t n_blocks_of(int64_t n_docs, int32_t block_docs) {
   return (n_docs + block_docs - 1) / block_docs;
 }
@@ -343,6 +362,37 @@ extern "C" int gsp_chunk_bounds(int64_t n_docs, int32_t V, int64_t doc_chunk, co
   const int64_t n_chunks = (n_docs + doc_chunk - 1) / doc_chunk;
   chunk_bounds_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, as_stream(stream)>>>(
       n_docs, V, doc_chunk, n_chunks, doc_ids, offsets, lengths, out);
+  GSP_CHECK_LAUNCH();
+  return GSP_OK;
+}
+
+extern "C" int gsp_index_head_rows(int32_t H, const int32_t* head_ids, const int64_t* offsets,
+                                   const int32_t* lengths, const int32_t* doc_ids, const void* weights,
+                                   int32_t wdtype, int64_t ld, void* rows, void* stream) {
+  GSP_REQUIRE(H >= 0 && ld >= 0 && (H == 0 || (head_ids && offsets && lengths && doc_ids && weights && rows)),
+              GSP_ERR_ARG, "gsp_index_head_rows: bad arguments");
+  if (H == 0) return GSP_OK;
+  cudaStream_t st = as_stream(stream);
+  switch (wdtype) {
+    case GSP_W_F32:
+      head_rows_kernel<float><<<unsigned(H), 256, 0, st>>>(H, head_ids, offsets, lengths, doc_ids,
+                                                           static_cast<const float*>(weights), ld,
+                                                           static_cast<float*>(rows));
+      break;
+    case GSP_W_BF16:
+      head_rows_kernel<__nv_bfloat16><<<unsigned(H), 256, 0, st>>>(
+          H, head_ids, offsets, lengths, doc_ids, static_cast<const __nv_bfloat16*>(weights), ld,
+          static_cast<__nv_bfloat16*>(rows));
+      break;
+    case GSP_W_U8:
+      head_rows_kernel<uint8_t><<<unsigned(H), 256, 0, st>>>(H, head_ids, offsets, lengths, doc_ids,
+                                                             static_cast<const uint8_t*>(weights), ld,
+                                                             static_cast<uint8_t*>(rows));
+      break;
+    default:
+      set_error("gsp_index_head_rows: unknown weight dtype %d", wdtype);
+      return GSP_ERR_ARG;
+  }
   GSP_CHECK_LAUNCH();
   return GSP_OK;
 }

@@ -3,28 +3,38 @@
 // Replaces src/triton_kernel.py:93-200 (_fast_scatter_add_kernel + torch.zeros +
 // torch.topk), src/triton_kernel_chunked.py:34-170 and src/fused_topk.py:33-160.
 //
-// Work decomposition.  Queries are cut into warp slots of QPW queries; a CTA holds
-// kWarps slots (one query group) and one document range (a run of whole index blocks).
-// Every warp owns fp32 accumulators acc[QPW][TILE] in shared memory for the current
-// document tile, so each accumulator cell has exactly one writer and no atomics are
-// needed.  Per tile the warp walks its "runs": the distinct terms of its queries in
-// ascending term id, each with the (query, weight) entries that use it.  A run streams
-// the term's postings that fall inside the tile (coalesced 32-wide loads from the cursor
-// kept per run; postings ascend by doc id so the tile boundary is a ballot) and applies
-// each posting to every entry of the run, so one posting load feeds all of the warp's
-// queries that contain the term.  Each cell therefore receives its contributions in
-// ascending (term id, slot) order with one fp32 rounding for the product and one for the
-// sum: results are bitwise reproducible and equal to the CPU oracle's canonical order.
+// Work decomposition.  Every query gets J_q "streams", J_q proportional to its estimated
+// work (its tail postings and dense head rows), one stream per resident warp in total.
+// The streams of a query take its document tiles in ascending order from a per-query
+// counter, so all queries sweep the document space at about the same relative pace and
+// the tiles in flight at any moment are a narrow window whose postings stay in L2.  A
+// stream keeps one candidate buffer (and a threshold that tightens) across its sweep.  A
+// warp whose streams are done helps the query with the most tiles left, with a spare
+// candidate buffer, so an estimate that is off costs no idle warps.  The tile is one index
+// block (1024 documents), so the window of every term's postings inside a tile is
+// [block_starts[b][t], block_starts[b+1][t]) with no search.  The warp owns the tile's
+// fp32 accumulators, so every (query, document) cell has exactly one writer, and the
+// result does not depend on which warp scored which tile.
 //
-// Selection.  After a tile every (query, tile) score is turned into a packed 64-bit key
-// (order-preserving score bits << 32 | ~doc id: larger is better, ties -> lower doc id)
-// and appended to the query's candidate buffer for this range if it is >= the query's
-// running threshold.  When the buffer would overflow, the owning warp radix-selects the
-// k-th largest key (8-bit digits, most significant first, early exit once the boundary
-// bucket is taken whole), compacts the buffer in place to exactly k keys and raises the
-// threshold to that boundary.  Every discarded key is below k kept keys of the same
-// query, so the final top-k is exact.  A merge kernel (select.cu) then reduces the
-// ranges' k-lists of each query to the answer.
+// Per tile:
+//  1. head terms (the index's densest terms, stored as dense rows): the warp keeps the
+//     1024 accumulators in registers (32 per lane) and streams each head row of the query
+//     with coalesced vector loads: acc += fl(q_w * w) for every document;
+//  2. the accumulators go to shared memory and the tail terms (all others), in ascending
+//     term id, are scattered into them: a run whose window is long (or that a query
+//     repeats) is streamed on its own, four 32-posting chunks in flight; consecutive short
+//     runs are flattened into full 32-lane chunks, and lanes that hit the same document
+//     (different terms) are applied in term order, one rank at a time (match_any);
+//  3. every score becomes a packed key (order-preserving score bits << 32 | ~doc id:
+//     larger is better, ties go to the lower doc id) and keys at or above the stream's
+//     threshold go to the stream's candidate buffer; on overflow the warp radix-selects
+//     the k-th largest key, compacts the buffer to exactly k keys and raises the
+//     threshold, which it also publishes (atomicMax) as a lower bound for the query's
+//     other streams.  A discarded key is beaten by k kept keys, so the final top-k
+//     (merge_kernel in select.cu) is exact.
+// Each cell therefore sums fl(q_w * d_w) in a fixed order -- head terms by term id, then
+// tail terms by term id, a repeated term in query-slot order -- with one fp32 rounding per
+// product and per sum: bitwise reproducible, and equal to the CPU oracle's canonical order.
 #include "common.cuh"
 
 #include <algorithm>
@@ -38,7 +48,10 @@ namespace gsp {
 
 constexpr int kWarps = 8;
 constexpr int kPlanThreads = 256;
-constexpr int kMaxEntriesPerSlot = 2048;
+constexpr int kMaxWidth = 4096;   // query slots (W) supported
+constexpr int kTile = 1024;       // documents per tile = index block
+constexpr int kLongRun = 48;      // tail windows at least this long are streamed on their own
+constexpr int kMaxHelp = 32;      // spare buffers one query can receive
 
 struct ScoreParams {
   const int32_t* doc_ids;
@@ -47,61 +60,65 @@ struct ScoreParams {
   const int64_t* offsets;
   const int32_t* lengths;
   const uint32_t* block_starts;
+  const void* head_rows;
+  int64_t head_ld;
   int64_t n_docs;
   int64_t doc_base;
   int32_t V;
-  int32_t block_docs;
   int32_t n_blocks;
   int32_t B;
-  int32_t W;
   int32_t k;
+  int32_t ecap;      // plan capacity per query (= W)
+  int32_t C;         // candidate buffer capacity per stream
+  int32_t n_streams; // streams over all queries (>= B)
+  int32_t n_spare;   // spare candidate buffers for helping warps
+  const int32_t* first_stream;   // [B+1]: streams of query q are [first_stream[q], first_stream[q+1])
+  int64_t* work;                 // [B]: estimated work of each query (plan output)
+  int32_t* next_block;           // [B]: next tile of each query (zeroed per call)
+  int32_t* help_count;           // [B]: spare buffers registered to each query (zeroed)
+  int32_t* spare_next;           // [1]: spare buffers handed out (zeroed)
+  int32_t* help_list;            // [B, kMaxHelp]: spare buffer ids of each query
+  // plan, per query: head entries and tail runs
+  const int32_t* n_head_e;
+  const uint16_t* head_h;
+  const float* head_w;
+  const float* head_scale;
+  const int32_t* n_runs;
   const int32_t* run_term;
   const uint32_t* run_base32;
   const uint16_t* run_end;
-  const uint8_t* ent_q;
+  const float* run_w0;
   const float* ent_w;
-  const int32_t* n_runs;
-  int32_t ecap;
-  int32_t C;
-  int32_t n_ranges;
-  int32_t n_slots;
   uint64_t* cand;
   int32_t* cand_cnt;
-  uint32_t* work_counter;
+  unsigned long long* gthr;   // per query: largest published lower bound of its k-th key
 };
 
 namespace {
 
 // ---------------------------------------------------------------------------- plan
-// One CTA per warp slot: gather the slot's (term, query, slot) triples, sort them by
-// that key (bitonic in shared memory) and emit runs of equal term ids.
+// One CTA per query: sort the query's (term, slot) pairs (bitonic in shared memory), then
+// split them into head entries (terms with a dense row) and tail runs (distinct other
+// terms, each with its entries in slot order).
 __global__ void __launch_bounds__(kPlanThreads)
 plan_kernel(const int32_t* __restrict__ qi, const float* __restrict__ qs, int32_t B, int32_t W,
-            int32_t V, int32_t qpw, int32_t ecap, int32_t npow2, const int64_t* __restrict__ offsets,
-            int32_t* __restrict__ run_term, uint32_t* __restrict__ run_base32,
-            uint16_t* __restrict__ run_end, uint8_t* __restrict__ ent_q, float* __restrict__ ent_w,
-            int32_t* __restrict__ n_runs) {
+            int32_t V, int32_t npow2, const int64_t* __restrict__ offsets,
+            const int32_t* __restrict__ head_slot, int32_t n_head, const float* __restrict__ term_scale,
+            ScoreParams p) {
   extern __shared__ uint64_t keys[];
-  __shared__ int32_t s_base;
-  __shared__ int32_t warp_cnt[kPlanThreads / 32];
-  const int32_t slot = blockIdx.x;
-  const int64_t q0 = int64_t(slot) * qpw;
-  const int32_t ne = qpw * W;
+  __shared__ int32_t s_head, s_tail, s_runs;
+  __shared__ int32_t w_head[kPlanThreads / 32], w_tail[kPlanThreads / 32], w_runs[kPlanThreads / 32];
+  const int32_t q = blockIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   for (int32_t i = threadIdx.x; i < npow2; i += blockDim.x) {
     uint64_t key = ~0ull;
-    if (i < ne) {
-      const int32_t qq = i / W, s = i - qq * W;
-      const int64_t q = q0 + qq;
-      if (q < B) {
-        const int32_t t = qi[q * W + s];
-        if (t >= 0 && t < V)
-          key = (uint64_t(uint32_t(t)) << 32) | (uint64_t(qq) << 16) | uint64_t(s);
-      }
+    if (i < W) {
+      const int32_t t = qi[int64_t(q) * W + i];
+      if (t >= 0 && t < V) key = (uint64_t(uint32_t(t)) << 32) | uint64_t(i);
     }
     keys[i] = key;
   }
   __syncthreads();
-  // bitonic sort, ascending
   for (int32_t size = 2; size <= npow2; size <<= 1) {
     for (int32_t stride = size >> 1; stride > 0; stride >>= 1) {
       for (int32_t i = threadIdx.x; i < npow2; i += blockDim.x) {
@@ -118,62 +135,145 @@ plan_kernel(const int32_t* __restrict__ qi, const float* __restrict__ qs, int32_
       __syncthreads();
     }
   }
-  // runs: a new run starts where the term id changes; ordinal by a running ballot scan
-  if (threadIdx.x == 0) s_base = 0;
+  if (threadIdx.x == 0) s_head = s_tail = s_runs = 0;
   __syncthreads();
-  const int64_t obase = int64_t(slot) * ecap;
+  const int64_t ob = int64_t(q) * p.ecap;
+  uint16_t* head_h = const_cast<uint16_t*>(p.head_h) + ob;
+  float* head_w = const_cast<float*>(p.head_w) + ob;
+  float* head_sc = const_cast<float*>(p.head_scale) + ob;
+  int32_t* run_term = const_cast<int32_t*>(p.run_term) + ob;
+  uint32_t* run_b32 = const_cast<uint32_t*>(p.run_base32) + ob;
+  uint16_t* run_end = const_cast<uint16_t*>(p.run_end) + ob;
+  float* run_w0 = const_cast<float*>(p.run_w0) + ob;
+  float* ent_w = const_cast<float*>(p.ent_w) + ob;
   for (int32_t i0 = 0; i0 < npow2; i0 += blockDim.x) {
     const int32_t i = i0 + threadIdx.x;
     const uint64_t key = keys[i];
     const bool valid = key != ~0ull;
-    const uint32_t t = uint32_t(key >> 32);
-    const bool start = valid && (i == 0 || uint32_t(keys[i - 1] >> 32) != t);
-    // block-wide exclusive count of starts before i
-    const uint32_t bal = __ballot_sync(FULL, start);
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    if (lane == 0) warp_cnt[wid] = __popc(bal);
+    const int32_t t = int32_t(key >> 32);
+    const int32_t s = int32_t(key & 0xFFFFFFFFu);
+    const int32_t h = (valid && n_head > 0) ? head_slot[t] : -1;
+    const bool is_head = valid && h >= 0;
+    const bool is_tail = valid && h < 0;
+    const bool start = is_tail && (i == 0 || int32_t(keys[i - 1] >> 32) != t);
+    const bool last = is_tail && (i + 1 >= npow2 || int32_t(keys[i + 1] >> 32) != t);
+    const uint32_t bh = __ballot_sync(FULL, is_head), bt = __ballot_sync(FULL, is_tail),
+                   bs = __ballot_sync(FULL, start);
+    if (lane == 0) {
+      w_head[wid] = __popc(bh);
+      w_tail[wid] = __popc(bt);
+      w_runs[wid] = __popc(bs);
+    }
     __syncthreads();
-    int32_t before = s_base;
-    for (int w = 0; w < wid; ++w) before += warp_cnt[w];
-    const int32_t rank = before + __popc(bal & lanemask_lt());
-    if (valid) {
-      const int32_t qq = int32_t((key >> 16) & 0xFFFF), s = int32_t(key & 0xFFFF);
-      ent_q[obase + i] = uint8_t(qq);
-      ent_w[obase + i] = qs[(q0 + qq) * W + s];
+    int32_t oh = s_head, ot = s_tail, orr = s_runs;
+    for (int w = 0; w < wid; ++w) {
+      oh += w_head[w];
+      ot += w_tail[w];
+      orr += w_runs[w];
+    }
+    const uint32_t lt = lanemask_lt();
+    const float qw = valid ? qs[int64_t(q) * W + s] : 0.f;
+    if (is_head) {
+      const int32_t e = oh + __popc(bh & lt);
+      head_h[e] = uint16_t(h);
+      head_w[e] = qw;
+      head_sc[e] = term_scale ? term_scale[t] : 1.0f;
+    }
+    if (is_tail) {
+      const int32_t e = ot + __popc(bt & lt);
+      const int32_t r = orr + __popc(bs & lt) - (start ? 0 : 1);
+      ent_w[e] = qw;
       if (start) {
-        run_term[obase + rank] = int32_t(t);
-        run_base32[obase + rank] = uint32_t(offsets[t] >> 5);
+        run_term[r] = t;
+        run_b32[r] = uint32_t(offsets[t] >> 5);
+        run_w0[r] = qw;
       }
-      // end of the run containing i is written by its last entry
-      const bool last = (i + 1 >= npow2) || keys[i + 1] == ~0ull || uint32_t(keys[i + 1] >> 32) != t;
-      if (last) run_end[obase + rank - (start ? 0 : 1)] = uint16_t(i + 1);
+      if (last) run_end[r] = uint16_t(e + 1);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      int32_t tot = 0;
-      for (int w = 0; w < kPlanThreads / 32; ++w) tot += warp_cnt[w];
-      s_base += tot;
+      for (int w = 0; w < kPlanThreads / 32; ++w) {
+        s_head += w_head[w];
+        s_tail += w_tail[w];
+        s_runs += w_runs[w];
+      }
     }
     __syncthreads();
   }
-  if (threadIdx.x == 0) n_runs[slot] = s_base;
+  if (threadIdx.x == 0) {
+    const_cast<int32_t*>(p.n_head_e)[q] = s_head;
+    const_cast<int32_t*>(p.n_runs)[q] = s_runs;
+  }
+  // work estimate: ~6 dense-row elements per tail posting, one per head row per document
+  int64_t wk = 0;
+  for (int32_t r = threadIdx.x; r < s_runs; r += blockDim.x) wk += p.lengths[run_term[r]];
+  __shared__ unsigned long long s_wk;
+  if (threadIdx.x == 0) s_wk = 0;
+  __syncthreads();
+  atomicAdd(&s_wk, (unsigned long long)wk);
+  __syncthreads();
+  if (threadIdx.x == 0) p.work[q] = 6 * int64_t(s_wk) + int64_t(s_head + 1) * p.n_docs;
+}
+
+// first_stream[q] = q + floor((S - B) * work_before(q) / total_work): every query gets at
+// least one stream, the rest in proportion to its work.  One CTA.
+__global__ void __launch_bounds__(1024) streams_kernel(const int64_t* __restrict__ work, int32_t B,
+                                                        int32_t S, int32_t* __restrict__ first) {
+  __shared__ long long s_carry, s_tot;
+  __shared__ long long warp_sum[32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  // total work
+  long long t = 0;
+  for (int32_t q = threadIdx.x; q < B; q += blockDim.x) t += work[q];
+  for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(FULL, t, o);
+  if (lane == 0) warp_sum[wid] = t;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    long long a = 0;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) a += warp_sum[w];
+    s_tot = a > 0 ? a : 1;
+    s_carry = 0;
+  }
+  __syncthreads();
+  const long long tot = s_tot;
+  const long long extra = (long long)S - B;
+  for (int32_t q0 = 0; q0 < B; q0 += blockDim.x) {
+    const int32_t q = q0 + threadIdx.x;
+    const long long v = q < B ? work[q] : 0;
+    long long x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(FULL, x, o);
+      if (lane >= o) x += y;
+    }
+    __syncthreads();
+    if (lane == 31) warp_sum[wid] = x;
+    __syncthreads();
+    long long before = s_carry;
+    for (int w = 0; w < wid; ++w) before += warp_sum[w];
+    before += x - v;
+    if (q < B) {
+      long long f = (long long)((double)extra * (double)before / (double)tot);
+      f = f < 0 ? 0 : (f > extra ? extra : f);   // first[] stays strictly increasing, < S
+      first[q] = int32_t(q + f);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      long long a = 0;
+      for (int w = 0; w < int(blockDim.x >> 5); ++w) a += warp_sum[w];
+      s_carry += a;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) first[B] = S;
 }
 
 // ---------------------------------------------------------------------------- scoring
 
-__host__ __device__ constexpr int align16(int x) { return (x + 15) / 16 * 16; }
-
-// Shared memory of one warp: its accumulator tile, a radix histogram and per-query
-// selection state.  Run and entry lists stay in global memory (L1-resident).
+// Shared memory of one warp: its accumulator tile and a radix histogram.
 struct WarpLayout {
-  int acc, hist, thr, cnt, total;
-  __host__ __device__ WarpLayout(int qpw, int tile) {
-    acc = 0;
-    hist = acc + qpw * tile * 4;
-    thr = hist + 256 * 4;
-    cnt = thr + align16(qpw * 8);
-    total = cnt + align16(qpw * 4);
-  }
+  static constexpr int acc = 0;
+  static constexpr int hist = kTile * 4;
+  static constexpr int total = hist + 256 * 4;
 };
 
 // Radix-select the k-th largest key of buf[0..n) (n > k, keys distinct), keep exactly the
@@ -243,29 +343,28 @@ __device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t 
   return prefix;
 }
 
-// acc[d - d0] += fl(qw * w) for one posting; the column test keeps a list that breaks the
-// ascending-doc-id invariant from ever addressing outside the tile.
-__device__ __forceinline__ void acc_add(float* __restrict__ row, int32_t col, uint32_t span, float qw,
+// acc[col] += fl(qw * w); the column test keeps a list that breaks the ascending-doc-id
+// invariant from ever addressing outside the tile.
+__device__ __forceinline__ void acc_add(float* __restrict__ acc, int32_t col, uint32_t span, float qw,
                                         float w) {
   if (uint32_t(col) < span) {
-    float* a = row + col;
+    float* a = acc + col;
     *a = __fadd_rn(*a, __fmul_rn(qw, w));
   }
 }
 
 constexpr int kUnroll = 4;   // posting chunks of one run in flight together
 
-// Apply the postings [wlo, whi) of one run to NE (1 or 2) entries held in registers, or to
-// every entry of the run from global memory when NE == 0.
-template <typename WT, int NE, int TILE>
+// Postings [0, n) of one run (pd/pw point at its window) applied to its NE entries (NE = 1
+// or 2 in registers; NE = 0: ne entries read from ew).  Every pass issues the loads of
+// kUnroll chunks (predicated past n) before it applies any, so a run costs one memory
+// round trip per 32 * kUnroll postings.
+template <typename WT, int NE>
 __device__ __forceinline__ void run_window(const int32_t* __restrict__ pd, const WT* __restrict__ pw,
                                            float scale, int32_t n, int32_t d0i, uint32_t span,
-                                           float* __restrict__ acc, int32_t q_a, float w_a, int32_t q_b,
-                                           float w_b, const uint8_t* __restrict__ eq,
+                                           float* __restrict__ acc, float w_a, float w_b,
                                            const float* __restrict__ ew, int32_t ne) {
   const int lane = lane_id();
-  float* row_a = acc + q_a * TILE;
-  float* row_b = acc + q_b * TILE;
   for (int32_t base = 0; base < n; base += 32 * kUnroll) {
     int32_t col[kUnroll];
     float w[kUnroll];
@@ -281,235 +380,345 @@ __device__ __forceinline__ void run_window(const int32_t* __restrict__ pd, const
     }
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      if constexpr (NE >= 1) acc_add(row_a, col[u], span, w_a, w[u]);
-      if constexpr (NE >= 2) acc_add(row_b, col[u], span, w_b, w[u]);
+      if constexpr (NE >= 1) acc_add(acc, col[u], span, w_a, w[u]);
+      if constexpr (NE >= 2) acc_add(acc, col[u], span, w_b, w[u]);
       if constexpr (NE == 0) {
-        for (int32_t e = 0; e < ne; ++e) acc_add(acc + int32_t(eq[e]) * TILE, col[u], span, ew[e], w[u]);
+        for (int32_t e = 0; e < ne; ++e) acc_add(acc, col[u], span, ew[e], w[u]);
       }
     }
   }
 }
 
-// Work items: (warp slot, document range).  Each warp takes items from a global counter
-// in order item = range * n_slots + slot, so warps running concurrently share a range and
-// its postings stay hot in L2.  Tiles are the index's document blocks, so every run's
-// window of postings in a tile is [block_starts[b][t], block_starts[b+1][t]).
-template <typename WT, int QPW, int TILE>
+// four consecutive weights of a dense head row, decoded to fp32
+template <typename WT>
+struct Vec4;
+template <>
+struct Vec4<float> {
+  __device__ __forceinline__ static float4 get(const float* p, float) {
+    return __ldg(reinterpret_cast<const float4*>(p));
+  }
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+  __device__ __forceinline__ static float4 get(const __nv_bfloat16* p, float) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                       __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+  }
+};
+template <>
+struct Vec4<uint8_t> {
+  __device__ __forceinline__ static float4 get(const uint8_t* p, float s) {
+    const uint32_t u = __ldg(reinterpret_cast<const unsigned int*>(p));
+    return make_float4(__fmul_rn(float(u & 255u), s), __fmul_rn(float((u >> 8) & 255u), s),
+                       __fmul_rn(float((u >> 16) & 255u), s), __fmul_rn(float(u >> 24), s));
+  }
+};
+
+__device__ __forceinline__ void fma4(float4& a, float qw, const float4 v) {
+  a.x = __fadd_rn(a.x, __fmul_rn(qw, v.x));
+  a.y = __fadd_rn(a.y, __fmul_rn(qw, v.y));
+  a.z = __fadd_rn(a.z, __fmul_rn(qw, v.z));
+  a.w = __fadd_rn(a.w, __fmul_rn(qw, v.w));
+}
+
+template <typename WT>
 __global__ void __launch_bounds__(kWarps * 32, 3)
 score_kernel(const ScoreParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int lane = lane_id(), wid = threadIdx.x >> 5;
-  const WarpLayout lay(QPW, TILE);
-  unsigned char* wsm = smem + size_t(wid) * lay.total;
-  float* acc = reinterpret_cast<float*>(wsm + lay.acc);
-  uint32_t* hist = reinterpret_cast<uint32_t*>(wsm + lay.hist);
-  uint64_t* kthr = reinterpret_cast<uint64_t*>(wsm + lay.thr);
-  int32_t* cnt = reinterpret_cast<int32_t*>(wsm + lay.cnt);
+  unsigned char* wsm = smem + size_t(wid) * WarpLayout::total;
+  float* acc = reinterpret_cast<float*>(wsm + WarpLayout::acc);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(wsm + WarpLayout::hist);
   const WT* __restrict__ wts = static_cast<const WT*>(p.weights);
+  const WT* __restrict__ hrows = static_cast<const WT*>(p.head_rows);
   const int32_t* __restrict__ doc_ids = p.doc_ids;
-  const uint32_t* __restrict__ bstarts = p.block_starts;
-  const int64_t n_items = int64_t(p.n_slots) * p.n_ranges;
-
+  const int32_t nwarps = int32_t(gridDim.x) * kWarps;
+  int32_t sid = blockIdx.x * kWarps + wid;
   for (;;) {
-    int64_t item = 0;
-    if (lane == 0) item = int64_t(atomicAdd(p.work_counter, 1u));
-    item = __shfl_sync(FULL, item, 0);
-    if (item >= n_items) break;
-    const int32_t slot = int32_t(item % p.n_slots);
-    const int32_t r = int32_t(item / p.n_slots);
-    const int64_t q0 = int64_t(slot) * QPW;
-    if (q0 >= p.B) continue;
-    const int64_t blk0 = int64_t(p.n_blocks) * r / p.n_ranges;
-    const int64_t blk1 = int64_t(p.n_blocks) * (r + 1) / p.n_ranges;
-    const int32_t nq = int32_t(min64(QPW, p.B - q0));
-    const int64_t pbase = int64_t(slot) * p.ecap;
-    const int32_t nr = p.n_runs[slot];
+    // next assignment: one of this warp's own streams, else a spare buffer for the query
+    // with the most tiles left
+    int32_t q = 0, list = 0;
+    if (sid < p.n_streams) {
+      int32_t lo_q = 0, hi_q = p.B - 1;   // last q with first_stream[q] <= sid
+      while (lo_q < hi_q) {
+        const int32_t mid = (lo_q + hi_q + 1) >> 1;
+        if (p.first_stream[mid] <= sid) lo_q = mid; else hi_q = mid - 1;
+      }
+      q = lo_q;
+      list = sid;
+      sid += nwarps;
+    } else {
+      int32_t best = -1, best_q = 0;
+      for (int32_t qq = lane; qq < p.B; qq += 32) {
+        const int32_t rem = p.n_blocks - __ldcg(p.next_block + qq);
+        if (rem > best) {
+          best = rem;
+          best_q = qq;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const int32_t ob = __shfl_xor_sync(FULL, best, o), oq = __shfl_xor_sync(FULL, best_q, o);
+        if (ob > best || (ob == best && oq < best_q)) {
+          best = ob;
+          best_q = oq;
+        }
+      }
+      if (best < 2) break;   // a tile or less left anywhere: the owners finish it
+      int32_t hb = 0, slot = 0;
+      if (lane == 0) {
+        hb = atomicAdd(p.spare_next, 1);
+        if (hb < p.n_spare) slot = atomicAdd(p.help_count + best_q, 1);
+      }
+      hb = __shfl_sync(FULL, hb, 0);
+      slot = __shfl_sync(FULL, slot, 0);
+      if (hb >= p.n_spare) break;
+      list = p.n_streams + hb;
+      if (slot >= kMaxHelp) {
+        if (lane == 0) p.cand_cnt[list] = 0;
+        break;
+      }
+      if (lane == 0) p.help_list[int64_t(best_q) * kMaxHelp + slot] = hb;
+      q = best_q;
+    }
+    const int64_t pbase = int64_t(q) * p.ecap;
+    const int32_t nhe = p.n_head_e[q];
+    const int32_t nr = p.n_runs[q];
+    const uint16_t* __restrict__ head_h = p.head_h + pbase;
+    const float* __restrict__ head_w = p.head_w + pbase;
+    const float* __restrict__ head_sc = p.head_scale + pbase;
     const int32_t* __restrict__ run_term = p.run_term + pbase;
     const uint32_t* __restrict__ run_b32 = p.run_base32 + pbase;
     const uint16_t* __restrict__ run_end = p.run_end + pbase;
-    const uint8_t* __restrict__ ent_q = p.ent_q + pbase;
+    const float* __restrict__ run_w0 = p.run_w0 + pbase;
     const float* __restrict__ ent_w = p.ent_w + pbase;
-    if (lane < QPW) {
-      kthr[lane] = 0ull;
-      cnt[lane] = 0;
-    }
-    __syncwarp();
+    uint64_t* __restrict__ buf = p.cand + int64_t(list) * p.C;
+    uint64_t thr = __ldcg(p.gthr + q);
+    int32_t nbuf = 0;
 
-    for (int64_t b = blk0; b < blk1; ++b) {
-      const int32_t d0i = int32_t(b * TILE);
-      const int32_t d1 = int32_t(min64((b + 1) * TILE, p.n_docs));
+    int32_t nb = 0;   // the claimed tile (lane 0)
+    if (lane == 0) nb = atomicAdd(p.next_block + q, 1);
+    for (;;) {
+      const int32_t b = __shfl_sync(FULL, nb, 0);
+      if (b >= p.n_blocks) break;
+      // claim the next tile now, so the atomic's round trip overlaps this tile's work
+      if (lane == 0) nb = atomicAdd(p.next_block + q, 1);
+      const int32_t d0i = b * kTile;
+      const int32_t d1 = int32_t(min64(int64_t(b + 1) * kTile, p.n_docs));
       const uint32_t span = uint32_t(d1 - d0i);
-      const uint32_t* __restrict__ brow = bstarts + b * int64_t(p.V);
-      float4* a4 = reinterpret_cast<float4*>(acc);
-#pragma unroll 4
-      for (int i = lane; i < QPW * TILE / 4; i += 32) a4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+      // 1. head rows, accumulators in registers: lane owns documents 128*i + 4*lane + j
+      float4 a[kTile / 128];
+#pragma unroll
+      for (int i = 0; i < kTile / 128; ++i) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int32_t e = 0; e < nhe; ++e) {
+        const int32_t h = head_h[e];
+        const float qw = head_w[e];
+        float sc = 1.0f;
+        if constexpr (std::is_same<WT, uint8_t>::value) sc = head_sc[e];
+        const WT* row = hrows + int64_t(h) * p.head_ld + d0i + 4 * lane;
+        float4 v[kTile / 128];
+#pragma unroll
+        for (int i = 0; i < kTile / 128; ++i) v[i] = Vec4<WT>::get(row + 128 * i, sc);
+#pragma unroll
+        for (int i = 0; i < kTile / 128; ++i) fma4(a[i], qw, v[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < kTile / 128; ++i) *reinterpret_cast<float4*>(acc + 128 * i + 4 * lane) = a[i];
       __syncwarp();
 
+      // 2. tail runs in ascending term id
+      const uint32_t* __restrict__ brow = p.block_starts + int64_t(b) * p.V;
       for (int32_t rb = 0; rb < nr; rb += 32) {
-        // this tile's window of up to 32 runs, one lane per run
         const int32_t ri = rb + lane;
-        uint32_t lo = 0, hi = 0;
-        int32_t e_lo = 0, e_hi = 0;
-        uint32_t b32 = 0;
+        uint32_t lo = 0, hi = 0, b32 = 0;
+        int32_t e0 = 0, ne = 0;
+        float w0 = 0.f, scale = 1.0f;
         if (ri < nr) {
           const int32_t t = run_term[ri];
           lo = __ldg(brow + t);
           hi = __ldg(brow + p.V + t);
-          e_lo = ri ? int32_t(run_end[ri - 1]) : 0;
-          e_hi = int32_t(run_end[ri]);
+          e0 = ri ? int32_t(run_end[ri - 1]) : 0;
+          ne = int32_t(run_end[ri]) - e0;
           b32 = run_b32[ri];
+          w0 = run_w0[ri];
+          if constexpr (std::is_same<WT, uint8_t>::value) scale = __ldg(p.term_scale + t);
         }
-        uint32_t am = __ballot_sync(FULL, hi > lo);
-        while (am) {
-          const int j = __ffs(am) - 1;
-          am &= am - 1;
-          const uint32_t wlo = __shfl_sync(FULL, lo, j), whi = __shfl_sync(FULL, hi, j);
-          const int32_t e0 = __shfl_sync(FULL, e_lo, j), e1 = __shfl_sync(FULL, e_hi, j);
-          const int64_t base = (int64_t(__shfl_sync(FULL, b32, j)) << 5) + wlo;
-          float scale = 1.0f;
-          if constexpr (std::is_same<WT, uint8_t>::value) scale = __ldg(p.term_scale + run_term[rb + j]);
-          const int32_t n = int32_t(whi - wlo), ne = e1 - e0;
-          const int32_t q_a = ent_q[e0];
-          const float w_a = ent_w[e0];
-          if (ne == 1) {
-            run_window<WT, 1, TILE>(doc_ids + base, wts + base, scale, n, d0i, span, acc, q_a, w_a, 0,
-                                    0.f, nullptr, nullptr, 0);
-          } else if (ne == 2) {
-            run_window<WT, 2, TILE>(doc_ids + base, wts + base, scale, n, d0i, span, acc, q_a, w_a,
-                                    ent_q[e0 + 1], ent_w[e0 + 1], nullptr, nullptr, 0);
-          } else {
-            run_window<WT, 0, TILE>(doc_ids + base, wts + base, scale, n, d0i, span, acc, 0, 0.f, 0,
-                                    0.f, ent_q + e0, ent_w + e0, ne);
+        const int32_t n = int32_t(hi - lo);
+        const uint32_t act = __ballot_sync(FULL, n > 0);
+        const uint32_t lng = __ballot_sync(FULL, n > 0 && (n >= kLongRun || ne > 1));
+        int c = 0;  // next run (lane) to process
+        while (c < 32) {
+          const uint32_t from = c ? ~((1u << c) - 1u) : FULL;
+          if (!(act & from)) break;
+          const uint32_t nl = lng & from;
+          const int next_long = nl ? __ffs(nl) - 1 : 32;
+          const uint32_t upto = next_long < 32 ? ((1u << next_long) - 1u) : FULL;
+          const uint32_t seg = act & ~lng & from & upto;
+          if (seg) {
+            // consecutive short runs flattened into full 32-lane chunks
+            const int m = __popc(seg);
+            const int src = lane < m ? int(__fns(seg, 0, lane + 1)) : 0;
+            const int32_t n_c = __shfl_sync(FULL, n, src);
+            const uint32_t lo_c = __shfl_sync(FULL, lo, src), b32_c = __shfl_sync(FULL, b32, src);
+            const float w_c = __shfl_sync(FULL, w0, src), s_c = __shfl_sync(FULL, scale, src);
+            const int32_t sz = lane < m ? n_c : 0;
+            int32_t incl = sz;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const int32_t y = __shfl_up_sync(FULL, incl, o);
+              if (lane >= o) incl += y;
+            }
+            const int32_t P = incl - sz;
+            const int32_t total = __shfl_sync(FULL, incl, 31);
+            for (int32_t F = 0; F < total; F += 32) {
+              const int32_t f = F + lane;
+              const bool valid = f < total;
+              const uint32_t bit = (lane < m && P >= F && P < F + 32) ? (1u << (P - F)) : 0u;
+              const uint32_t S = __reduce_or_sync(FULL, bit);
+              const int jF = __popc(__ballot_sync(FULL, lane < m && P <= F)) - 1;
+              int j = jF + __popc(S & (lanemask_lt() | (1u << lane)) & ~1u);
+              j = valid ? j : 0;
+              const int32_t Pj = __shfl_sync(FULL, P, j);
+              const uint32_t loj = __shfl_sync(FULL, lo_c, j), bj = __shfl_sync(FULL, b32_c, j);
+              const float wj = __shfl_sync(FULL, w_c, j), sj = __shfl_sync(FULL, s_c, j);
+              int32_t col = -1;
+              float wv = 0.f;
+              if (valid) {
+                const int64_t pos = (int64_t(bj) << 5) + loj + (f - Pj);
+                col = __ldg(doc_ids + pos) - d0i;
+                wv = WDecode<WT>::get(wts, pos, sj);
+              }
+              // lanes on the same document (different terms) apply in term (= lane) order
+              const int32_t dkey = (valid && uint32_t(col) < span) ? col : -1 - lane;
+              const uint32_t peers = __match_any_sync(FULL, dkey);
+              const int rank = __popc(peers & lanemask_lt());
+              const int top = int(__reduce_max_sync(FULL, uint32_t(rank)));
+              for (int rr = 0; rr <= top; ++rr) {
+                if (rank == rr) acc_add(acc, col, span, wj, wv);
+                __syncwarp();
+              }
+            }
           }
+          if (next_long >= 32) break;
+          // one long (or multi-entry) run
+          const int jl = next_long;
+          const int32_t nl_n = __shfl_sync(FULL, n, jl);
+          const uint32_t lo_l = __shfl_sync(FULL, lo, jl), b32_l = __shfl_sync(FULL, b32, jl);
+          const int32_t e0_l = __shfl_sync(FULL, e0, jl), ne_l = __shfl_sync(FULL, ne, jl);
+          const float w0_l = __shfl_sync(FULL, w0, jl), sc_l = __shfl_sync(FULL, scale, jl);
+          const int64_t base = (int64_t(b32_l) << 5) + lo_l;
+          if (ne_l == 1) {
+            run_window<WT, 1>(doc_ids + base, wts + base, sc_l, nl_n, d0i, span, acc, w0_l, 0.f, nullptr, 0);
+          } else if (ne_l == 2) {
+            run_window<WT, 2>(doc_ids + base, wts + base, sc_l, nl_n, d0i, span, acc, w0_l, ent_w[e0_l + 1],
+                              nullptr, 0);
+          } else {
+            run_window<WT, 0>(doc_ids + base, wts + base, sc_l, nl_n, d0i, span, acc, 0.f, 0.f, ent_w + e0_l,
+                              ne_l);
+          }
+          c = jl + 1;
         }
       }
       __syncwarp();
 
-      // fused selection of this tile
-      for (int32_t qq = 0; qq < nq; ++qq) {
-        uint64_t* __restrict__ buf = p.cand + ((q0 + qq) * p.n_ranges + r) * int64_t(p.C);
-        uint64_t thr = kthr[qq];
-        int32_t n = cnt[qq];
-        for (int32_t c0 = 0; c0 < d1 - d0i; c0 += 32) {
-          const int32_t col = c0 + lane;
-          const bool valid = d0i + col < d1;
-          const float s = acc[qq * TILE + (valid ? col : 0)];
-          const uint64_t key = pack_key(s, uint32_t(p.doc_base + d0i + col));
-          bool pass = valid && key >= thr;
-          uint32_t bal = __ballot_sync(FULL, pass);
-          if (!bal) continue;
-          if (n + __popc(bal) > p.C) {
-            thr = warp_compact(buf, n, p.k, hist);
-            n = p.k;
-            pass = pass && key >= thr;
-            bal = __ballot_sync(FULL, pass);
-          }
-          if (pass) buf[n + __popc(bal & lanemask_lt())] = key;
-          n += __popc(bal);
+      // 3. fused selection (a float comparison rejects almost every document first)
+      thr = max(thr, uint64_t(__ldcg(p.gthr + q)));
+      const uint32_t thi = uint32_t(thr >> 32);
+      const float thr_s = thi < 0x00800000u ? -INFINITY : fkey_inv(thi);
+      for (int32_t c0 = 0; c0 < int32_t(span); c0 += 32) {
+        const int32_t col = c0 + lane;
+        const bool valid = col < int32_t(span);
+        const float s = acc[valid ? col : 0];
+        if (!__ballot_sync(FULL, valid && s >= thr_s)) continue;
+        const uint64_t key = pack_key(s, uint32_t(p.doc_base + d0i + col));
+        bool pass = valid && key >= thr;
+        uint32_t bal = __ballot_sync(FULL, pass);
+        if (!bal) continue;
+        if (nbuf + __popc(bal) > p.C) {
+          thr = warp_compact(buf, nbuf, p.k, hist);
+          nbuf = p.k;
+          if (lane == 0) atomicMax(p.gthr + q, (unsigned long long)thr);
+          pass = pass && key >= thr;
+          bal = __ballot_sync(FULL, pass);
         }
-        __syncwarp();
-        if (lane == 0) {
-          kthr[qq] = thr;
-          cnt[qq] = n;
-        }
-        __syncwarp();
+        if (pass) buf[nbuf + __popc(bal & lanemask_lt())] = key;
+        nbuf += __popc(bal);
       }
+      __syncwarp();
     }
-
-    for (int32_t qq = 0; qq < nq; ++qq) {
-      uint64_t* __restrict__ buf = p.cand + ((q0 + qq) * p.n_ranges + r) * int64_t(p.C);
-      int32_t n = cnt[qq];
-      if (n > p.k) {
-        warp_compact(buf, n, p.k, hist);
-        n = p.k;
-      }
-      if (lane == 0) p.cand_cnt[(q0 + qq) * p.n_ranges + r] = n;
+    if (nbuf > p.k) {
+      const uint64_t t2 = warp_compact(buf, nbuf, p.k, hist);
+      nbuf = p.k;
+      if (lane == 0) atomicMax(p.gthr + q, (unsigned long long)t2);
     }
+    if (lane == 0) p.cand_cnt[list] = nbuf;
     __syncwarp();
   }
 }
 
 struct Cfg {
-  int qpw = 0, tile = 0, ecap = 0, npow2 = 0, n_groups = 0, n_slots = 0, R = 0, C = 0;
-  int wbytes = 0, smem = 0, ctas_per_sm = 0, grid = 0;
-  int64_t n_blocks = 0, kk = 0;
-  int64_t off_run_term = 0, off_run_b32 = 0, off_run_end = 0, off_ent_q = 0, off_ent_w = 0, off_nruns = 0,
-          off_cand = 0, off_cnt = 0, off_counter = 0, total = 0;
+  int npow2 = 0, S = 0, H = 0, C = 0, smem = 0, ctas_per_sm = 0, grid = 0;
+  int64_t ecap = 0, n_blocks = 0, kk = 0;
+  int64_t off_nhe = 0, off_hh = 0, off_hw = 0, off_hs = 0, off_nruns = 0, off_rterm = 0, off_rb32 = 0,
+          off_rend = 0, off_rw0 = 0, off_entw = 0, off_cand = 0, off_cnt = 0, off_first = 0,
+          off_work = 0, off_hlist = 0, off_zero = 0, zero_bytes = 0, total = 0;
 };
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
-int warp_bytes(int qpw, int tile) { return WarpLayout(qpw, tile).total; }
-
-// (queries per warp, tile) shapes that are compiled, preferred first for each tile
-static const int kShapes[][2] = {{2, 1024}, {4, 1024}, {1, 1024}, {2, 2048}, {1, 2048}, {1, 4096},
-                                 {4, 512},  {2, 512},  {4, 256}};
-
-// Workspace layout of one call for the configured shape and range count.
+// Workspace layout of one call for the configured stream count.
 void set_layout(Cfg& c, int64_t B) {
   int64_t o = 0;
-  c.off_run_term = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 4);
-  c.off_run_b32 = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 4);
-  c.off_run_end = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 2);
-  c.off_ent_q = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 1);
-  c.off_ent_w = o; o = align256(o + int64_t(c.n_slots) * c.ecap * 4);
-  c.off_nruns = o; o = align256(o + int64_t(c.n_slots) * 4);
-  c.off_cand = o; o = align256(o + B * int64_t(c.R) * c.C * 8);
-  c.off_cnt = o; o = align256(o + B * int64_t(c.R) * 4);
-  c.off_counter = o; o = align256(o + 4);
+  const int64_t E = B * c.ecap;
+  c.off_nhe = o; o = align256(o + B * 4);
+  c.off_hh = o; o = align256(o + E * 2);
+  c.off_hw = o; o = align256(o + E * 4);
+  c.off_hs = o; o = align256(o + E * 4);
+  c.off_nruns = o; o = align256(o + B * 4);
+  c.off_rterm = o; o = align256(o + E * 4);
+  c.off_rb32 = o; o = align256(o + E * 4);
+  c.off_rend = o; o = align256(o + E * 2);
+  c.off_rw0 = o; o = align256(o + E * 4);
+  c.off_entw = o; o = align256(o + E * 4);
+  c.off_cand = o; o = align256(o + int64_t(c.S + c.H) * c.C * 8);
+  c.off_cnt = o; o = align256(o + int64_t(c.S + c.H) * 4);
+  c.off_first = o; o = align256(o + (B + 1) * 4);
+  c.off_work = o; o = align256(o + B * 8);
+  c.off_hlist = o; o = align256(o + B * kMaxHelp * 4);
+  // cleared by every call: thresholds [B] u64, next tile [B], help counts [B], spare counter
+  c.off_zero = o; c.zero_bytes = B * 8 + B * 4 + B * 4 + 4; o = align256(o + c.zero_bytes);
   c.total = o;
 }
 
 int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) {
   GSP_REQUIRE(ix && ix->V > 0 && ix->n_docs >= 0 && ix->block_docs > 0, GSP_ERR_ARG,
               "score: bad index view");
-  GSP_REQUIRE(B >= 0 && W >= 1 && W <= 65535 && k >= 1, GSP_ERR_ARG,
-              "score: bad batch shape (B=%lld W=%lld k=%lld)", (long long)B, (long long)W, (long long)k);
-  GSP_REQUIRE(W <= kMaxEntriesPerSlot, GSP_ERR_UNSUPPORTED,
-              "score: query width %lld exceeds the supported maximum %d", (long long)W,
-              kMaxEntriesPerSlot);
+  GSP_REQUIRE(ix->block_docs == kTile, GSP_ERR_UNSUPPORTED,
+              "score: the scorer needs index blocks of %d documents (this index has %d)", kTile,
+              ix->block_docs);
+  GSP_REQUIRE(B >= 0 && W >= 1 && k >= 1, GSP_ERR_ARG, "score: bad batch shape (B=%lld W=%lld k=%lld)",
+              (long long)B, (long long)W, (long long)k);
+  GSP_REQUIRE(W <= kMaxWidth, GSP_ERR_UNSUPPORTED,
+              "score: query width %lld exceeds the supported maximum %d", (long long)W, kMaxWidth);
+  GSP_REQUIRE(ix->n_head >= 0 && ix->n_head <= 65535 && (ix->n_head == 0 || (ix->head_slot && ix->head_rows)),
+              GSP_ERR_ARG, "score: bad head rows");
   c.kk = std::min<int64_t>(k, ix->n_docs);
   GSP_REQUIRE(c.kk <= 8192, GSP_ERR_UNSUPPORTED, "score: top_k %lld exceeds the supported maximum 8192",
               (long long)c.kk);
-  const int smem_max = max_smem_optin();
   const int sms = num_sms();
-  // GSP_SCORE_QPW overrides the choice (tuning)
-  int want_q = 0;
-  if (const char* e = getenv("GSP_SCORE_QPW")) want_q = atoi(e);
-  c.qpw = 0;
-  c.tile = ix->block_docs;
-  for (const auto& sh : kShapes) {
-    const int qpw = sh[0], tile = sh[1];
-    if (tile != c.tile || (want_q && qpw != want_q)) continue;
-    if (qpw * W > kMaxEntriesPerSlot) continue;
-    const int ecap = int(qpw * W);
-    const int wb = warp_bytes(qpw, tile);
-    if (wb * kWarps <= smem_max) {
-      c.qpw = qpw;
-      c.ecap = ecap;
-      c.wbytes = wb;
-      break;
-    }
-  }
-  GSP_REQUIRE(c.qpw > 0, GSP_ERR_UNSUPPORTED,
-              "score: no scoring kernel for index block size %d with query width %lld",
-              ix->block_docs, (long long)W);
-  c.smem = c.wbytes * kWarps;
-  c.ctas_per_sm = std::max(1, std::min(8, (228 * 1024) / (c.smem + 1024)));
+  c.ecap = W;
+  c.smem = WarpLayout::total * kWarps;
+  c.ctas_per_sm = 3;
   c.npow2 = kPlanThreads;
-  while (c.npow2 < c.qpw * W) c.npow2 <<= 1;
-  const int64_t slots_needed = (B + c.qpw - 1) / c.qpw;
-  c.n_groups = int((slots_needed + kWarps - 1) / kWarps);
-  c.n_slots = c.n_groups * kWarps;
-  c.n_blocks = (ix->n_docs + c.tile - 1) / c.tile;
-  // about four work items per resident warp, ranges of whole blocks
+  while (c.npow2 < W) c.npow2 <<= 1;
+  c.n_blocks = (ix->n_docs + kTile - 1) / kTile;
+  // one stream per resident warp (at least one per query)
   const int64_t warps = int64_t(sms) * c.ctas_per_sm * kWarps;
-  int64_t R = std::max<int64_t>(1, (4 * warps + slots_needed - 1) / std::max<int64_t>(1, slots_needed));
-  R = std::min<int64_t>(R, std::max<int64_t>(1, c.n_blocks));
-  R = std::min<int64_t>(R, 4096);
-  c.R = int(R);
-  c.grid = int(std::min<int64_t>(int64_t(sms) * c.ctas_per_sm,
-                                 (int64_t(c.n_slots) * c.R + kWarps - 1) / kWarps));
+  c.S = int(std::max<int64_t>(warps, B));
+  c.H = c.S;
+  c.grid = int(std::min<int64_t>(int64_t(sms) * c.ctas_per_sm, (c.S + kWarps - 1) / kWarps));
   c.C = int(((std::max<int64_t>(2 * c.kk, c.kk + 256) + 31) / 32) * 32);
   set_layout(c, B);
   return GSP_OK;
@@ -528,9 +737,9 @@ Profile& profile() {
   return p;
 }
 
-template <typename WT, int QPW, int TILE>
+template <typename WT>
 int launch_score(const ScoreParams& p, const Cfg& c, cudaStream_t st) {
-  auto kern = score_kernel<WT, QPW, TILE>;
+  auto kern = score_kernel<WT>;
   GSP_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem));
   Profile& pr = profile();
   std::pair<cudaEvent_t, cudaEvent_t>* evp = nullptr;
@@ -552,18 +761,6 @@ int launch_score(const ScoreParams& p, const Cfg& c, cudaStream_t st) {
   if (evp) GSP_CUDA(cudaEventRecord(evp->second, st));
   return GSP_OK;
 }
-
-template <typename WT>
-int dispatch_tile(const ScoreParams& p, const Cfg& c, cudaStream_t st) {
-#define GSP_CASE(Q, T) \
-  if (c.qpw == Q && c.tile == T) return launch_score<WT, Q, T>(p, c, st);
-  GSP_CASE(2, 1024) GSP_CASE(4, 1024) GSP_CASE(1, 1024) GSP_CASE(2, 2048) GSP_CASE(1, 2048)
-  GSP_CASE(1, 4096) GSP_CASE(4, 512) GSP_CASE(2, 512) GSP_CASE(4, 256)
-#undef GSP_CASE
-  set_error("score: no kernel instantiated for qpw=%d tile=%d", c.qpw, c.tile);
-  return GSP_ERR_UNSUPPORTED;
-}
-
 
 }  // namespace
 }  // namespace gsp
@@ -589,6 +786,8 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
               "gsp_score_topk: global doc ids must stay below 2^32 - 1");
   if (B == 0 || c.kk == 0) return GSP_OK;
   GSP_REQUIRE(qi && qs && out_scores && out_ids, GSP_ERR_ARG, "gsp_score_topk: null argument");
+  GSP_REQUIRE(ix->n_head == 0 || ix->head_ld >= c.n_blocks * kTile, GSP_ERR_ARG,
+              "gsp_score_topk: head rows shorter than the block-padded document count");
   char* w = static_cast<char*>(ws);
   ScoreParams p;
   p.doc_ids = ix->doc_ids;
@@ -597,48 +796,59 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.offsets = ix->offsets;
   p.lengths = ix->lengths;
   p.block_starts = ix->block_starts;
+  p.head_rows = ix->head_rows;
+  p.head_ld = ix->head_ld;
   p.n_docs = ix->n_docs;
   p.doc_base = ix->doc_base;
   p.V = ix->V;
-  p.block_docs = ix->block_docs;
   p.n_blocks = int32_t(c.n_blocks);
   p.B = int32_t(B);
-  p.W = int32_t(W);
   p.k = int32_t(c.kk);
-  p.run_term = reinterpret_cast<int32_t*>(w + c.off_run_term);
-  p.run_base32 = reinterpret_cast<uint32_t*>(w + c.off_run_b32);
-  p.run_end = reinterpret_cast<uint16_t*>(w + c.off_run_end);
-  p.ent_q = reinterpret_cast<uint8_t*>(w + c.off_ent_q);
-  p.ent_w = reinterpret_cast<float*>(w + c.off_ent_w);
-  p.n_runs = reinterpret_cast<int32_t*>(w + c.off_nruns);
-  p.ecap = c.ecap;
+  p.ecap = int32_t(c.ecap);
   p.C = c.C;
-  p.n_ranges = c.R;
-  p.n_slots = c.n_slots;
+  p.n_streams = c.S;
+  p.n_spare = c.H;
+  p.n_head_e = reinterpret_cast<int32_t*>(w + c.off_nhe);
+  p.head_h = reinterpret_cast<uint16_t*>(w + c.off_hh);
+  p.head_w = reinterpret_cast<float*>(w + c.off_hw);
+  p.head_scale = reinterpret_cast<float*>(w + c.off_hs);
+  p.n_runs = reinterpret_cast<int32_t*>(w + c.off_nruns);
+  p.run_term = reinterpret_cast<int32_t*>(w + c.off_rterm);
+  p.run_base32 = reinterpret_cast<uint32_t*>(w + c.off_rb32);
+  p.run_end = reinterpret_cast<uint16_t*>(w + c.off_rend);
+  p.run_w0 = reinterpret_cast<float*>(w + c.off_rw0);
+  p.ent_w = reinterpret_cast<float*>(w + c.off_entw);
   p.cand = reinterpret_cast<uint64_t*>(w + c.off_cand);
   p.cand_cnt = reinterpret_cast<int32_t*>(w + c.off_cnt);
-  p.work_counter = reinterpret_cast<uint32_t*>(w + c.off_counter);
-  GSP_CUDA(cudaMemsetAsync(p.work_counter, 0, sizeof(uint32_t), st));
+  p.first_stream = reinterpret_cast<int32_t*>(w + c.off_first);
+  p.work = reinterpret_cast<int64_t*>(w + c.off_work);
+  p.help_list = reinterpret_cast<int32_t*>(w + c.off_hlist);
+  p.gthr = reinterpret_cast<unsigned long long*>(w + c.off_zero);
+  p.next_block = reinterpret_cast<int32_t*>(w + c.off_zero + B * 8);
+  p.help_count = p.next_block + B;
+  p.spare_next = p.help_count + B;
+  GSP_CUDA(cudaMemsetAsync(w + c.off_zero, 0, size_t(c.zero_bytes), st));
 
   const size_t plan_smem = size_t(c.npow2) * 8;
   GSP_CUDA(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(plan_smem)));
-  plan_kernel<<<unsigned(c.n_slots), kPlanThreads, plan_smem, st>>>(
-      qi, qs, int32_t(B), int32_t(W), ix->V, c.qpw, c.ecap, c.npow2, ix->offsets,
-      const_cast<int32_t*>(p.run_term), const_cast<uint32_t*>(p.run_base32), const_cast<uint16_t*>(p.run_end), const_cast<uint8_t*>(p.ent_q), const_cast<float*>(p.ent_w),
-      const_cast<int32_t*>(p.n_runs));
+  plan_kernel<<<unsigned(B), kPlanThreads, plan_smem, st>>>(
+      qi, qs, int32_t(B), int32_t(W), ix->V, c.npow2, ix->offsets, ix->head_slot, ix->n_head,
+      ix->wdtype == GSP_W_U8 ? ix->term_scale : nullptr, p);
+  GSP_CHECK_LAUNCH();
+  streams_kernel<<<1, 1024, 0, st>>>(p.work, int32_t(B), c.S, const_cast<int32_t*>(p.first_stream));
   GSP_CHECK_LAUNCH();
 
   if (c.n_blocks > 0) {
     switch (ix->wdtype) {
-      case GSP_W_F32: rc = dispatch_tile<float>(p, c, st); break;
-      case GSP_W_BF16: rc = dispatch_tile<__nv_bfloat16>(p, c, st); break;
-      case GSP_W_U8: rc = dispatch_tile<uint8_t>(p, c, st); break;
+      case GSP_W_F32: rc = launch_score<float>(p, c, st); break;
+      case GSP_W_BF16: rc = launch_score<__nv_bfloat16>(p, c, st); break;
+      case GSP_W_U8: rc = launch_score<uint8_t>(p, c, st); break;
       default: set_error("gsp_score_topk: unknown weight dtype %d", ix->wdtype); return GSP_ERR_ARG;
     }
     if (rc) return rc;
   }
-  return merge_topk_device(p.cand, B, c.R, int64_t(c.R) * c.C, c.C, p.cand_cnt, c.R, nullptr, c.kk,
-                           out_scores, out_ids, out_keys, st);
+  return merge_streams_device(p.cand, B, p.first_stream, p.help_list, p.help_count, kMaxHelp, c.S, c.C,
+                              p.cand_cnt, c.kk, out_scores, out_ids, out_keys, st);
 }
 
 extern "C" int gsp_profile_enable(int on) {
@@ -685,9 +895,9 @@ extern "C" int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const
 // application (for example a search engine that loads this library as a native plug-in
 // through a C FFI) that hands the library only its input and output buffers and owns no
 // device allocator to lend it a workspace.  gsp_score_topk_noalloc serves them: its
-// scratch (query plan, candidate buffers, work counter) lives in the file-scope array
-// below, which the CUDA runtime places on every GPU that loads this library and keeps
-// until the process exits.
+// scratch (query plan, candidate buffers, work counter, thresholds) lives in the
+// file-scope array below, which the CUDA runtime places on every GPU that loads this
+// library and keeps until the process exits.
 constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;   // 32 MiB per GPU
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -722,23 +932,27 @@ extern "C" int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* q
   Cfg c;
   int rc = make_cfg(ix, B, W, k, c);
   if (rc) return rc;
-  // fewer document ranges shrink the candidate buffers; the result does not depend on
-  // the range count, only the parallelism does
-  while (c.total > int64_t(kNoAllocScratchBytes) && c.R > 1) {
-    c.R = std::max(1, c.R / 2);
+  // fewer streams shrink the candidate buffers; the result does not depend on the stream
+  // count, only the parallelism does
+  while (c.total > int64_t(kNoAllocScratchBytes) && (c.S > B || c.H > 0)) {
+    if (c.H > 0) {
+      c.H /= 2;
+    } else {
+      c.S = int(std::max<int64_t>(B, c.S / 2));
+    }
     set_layout(c, B);
   }
   GSP_REQUIRE(c.total <= int64_t(kNoAllocScratchBytes), GSP_ERR_UNSUPPORTED,
               "gsp_score_topk_noalloc: this batch needs %lld bytes of scratch, more than the "
               "fixed %lld (lower the batch size or top_k, or use gsp_score_topk with a workspace)",
               (long long)c.total, (long long)kNoAllocScratchBytes);
-  c.grid = int(std::min<int64_t>(int64_t(num_sms()) * c.ctas_per_sm,
-                                 (int64_t(c.n_slots) * c.R + kWarps - 1) / kWarps));
+  c.grid = int(std::min<int64_t>(int64_t(num_sms()) * c.ctas_per_sm, (c.S + kWarps - 1) / kWarps));
   void* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
   // Every buffer in the scratch is written before it is read within a call except the
-  // work counter, which score_with_cfg clears on the stream; the array keeps the previous
-  // call's contents otherwise.
+  // per-query thresholds and tile counters and the spare-buffer counters, which
+  // score_with_cfg clears on the stream; the array keeps the previous call's contents
+  // otherwise.
   return score_with_cfg(ix, qi, qs, B, W, c, out_scores, out_ids, out_keys, scratch, as_stream(stream));
 }

@@ -30,7 +30,7 @@ W_F32, W_BF16, W_U8 = 0, 1, 2
 EXPORTS = (
     "gsp_last_error", "gsp_version", "gsp_scan_i32", "gsp_scan_ws_bytes", "gsp_synth_nnz",
     "gsp_synth_fill", "gsp_index_ws_bytes", "gsp_index_count", "gsp_index_fill",
-    "gsp_index_quantize", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
+    "gsp_index_quantize", "gsp_index_head_rows", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
     "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_profile_enable", "gsp_profile_collect", "gsp_merge_topk",
     "gsp_compacted_ws_bytes", "gsp_compacted_topk",
 )
@@ -44,6 +44,8 @@ class IndexView(ctypes.Structure):
         ("doc_ids", ctypes.c_void_p), ("weights", ctypes.c_void_p),
         ("term_scale", ctypes.c_void_p), ("offsets", ctypes.c_void_p),
         ("lengths", ctypes.c_void_p), ("block_starts", ctypes.c_void_p),
+        ("n_head", ctypes.c_int32), ("pad2_", ctypes.c_int32), ("head_slot", ctypes.c_void_p),
+        ("head_rows", ctypes.c_void_p), ("head_ld", ctypes.c_int64),
     ]
 
 
@@ -82,6 +84,7 @@ def lib() -> ctypes.CDLL:
             "gsp_index_fill": (ctypes.c_int, [i64, i32, i32, p, p, p, p, p, p, i64, p, p, p, p,
                                               i64, p]),
             "gsp_index_quantize": (ctypes.c_int, [i32, i64, p, p, p, p, i32, p, p, p]),
+            "gsp_index_head_rows": (ctypes.c_int, [i32, p, p, p, p, p, i32, i64, p, p]),
             "gsp_check_sorted": (ctypes.c_int, [i32, p, p, p, ctypes.POINTER(i64), p]),
             "gsp_chunk_bounds": (ctypes.c_int, [i64, i32, i64, p, p, p, p, p]),
             "gsp_score_ws_bytes": (i64, [ctypes.POINTER(IndexView), i64, i64, i64]),

@@ -45,6 +45,15 @@ class ShardLayout:
         return [min(k, s) for s in self.sizes()]
 
 
+def global_head(index, n_head: int, group=None) -> torch.Tensor:
+    """The corpus-wide head set (the n_head longest posting lists summed over all shards,
+    ties to the lower term id), so every shard sums a document's terms in the same order."""
+    lengths = index.lengths.to(torch.int64).clone()
+    dist.all_reduce(lengths, group=group)
+    top = torch.sort(-lengths, stable=True).indices[:n_head]
+    return top.sort().values.to(torch.int32)
+
+
 def gather_candidates(local_keys: torch.Tensor, k: int, group=None) -> torch.Tensor:
     """All-gather each rank's [B, k_local] int64 keys, zero-padded to [B, k], into
     [world, B, k] on every rank (one collective)."""

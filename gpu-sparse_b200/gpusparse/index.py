@@ -9,7 +9,11 @@ keeps:
   ``term_scale`` (uint8 mode: weight = q * term_scale[t]);
 * ``block_starts`` int32 [n_blocks+1, V]: postings of term t with doc id < b*block_docs,
   the doc-range blocks a scorer uses to start mid-list without searching;
-* ``doc_base``: global id of local document 0 when the index is one doc-range shard.
+* ``doc_base``: global id of local document 0 when the index is one doc-range shard;
+* ``head_ids`` / ``head_slot`` / ``head_rows``: the N_HEAD terms with the longest posting
+  lists, also stored as dense rows [n_head, ld] (the weight of the term in every document,
+  0 where absent) that the scorer streams with coalesced vector loads into register
+  accumulators instead of scattering their postings.
 
 Builders run on the GPU (csrc/build.cu); the CSR is only copied host -> device.
 """
@@ -26,6 +30,7 @@ from . import _lib as L
 
 BLOCK_SIZE = 32          # posting lists are padded to a warp (src/gpu_inverted_index.py:18)
 BLOCK_DOCS = 1024        # documents per block_starts row = the scorer's document tile
+N_HEAD = 32              # densest terms scored from dense rows instead of posting lists
 VOCAB_SIZE = 30522       # src/run_correctness_verification.py:28
 
 
@@ -47,6 +52,10 @@ class GPUInvertedIndex:
     block_starts: Optional[torch.Tensor] = None
     block_docs: int = BLOCK_DOCS
     doc_base: int = 0
+    head_ids: Optional[torch.Tensor] = None
+    head_slot: Optional[torch.Tensor] = None
+    head_rows: Optional[torch.Tensor] = None
+    head_ld: int = 0
     _view: object = field(default=None, repr=False, compare=False)
 
 
@@ -62,7 +71,7 @@ def _dev(device) -> torch.device:
 def build_from_csr_tensors(indptr: torch.Tensor, indices: torch.Tensor, data: torch.Tensor,
                            vocab_size: int, device=None, weight_dtype: str = "fp32",
                            doc_base: int = 0, keep_fp32: bool = True,
-                           block_docs: int = BLOCK_DOCS) -> GPUInvertedIndex:
+                           block_docs: int = BLOCK_DOCS, head_ids=None) -> GPUInvertedIndex:
     """Build from device CSR tensors (indptr int64 [N+1], indices int32, data fp32)."""
     device = _dev(device if device is not None else indptr.device)
     indptr = indptr.to(device=device, dtype=torch.int64).contiguous()
@@ -100,6 +109,8 @@ def build_from_csr_tensors(indptr: torch.Tensor, indices: torch.Tensor, data: to
                                block_docs=block_docs, doc_base=int(doc_base))
         if weight_dtype != "fp32":
             quantize_(idx, weight_dtype, keep_fp32=keep_fp32)
+        if block_docs == BLOCK_DOCS:
+            ensure_head(idx, head_ids=head_ids)
     return idx
 
 
@@ -127,6 +138,7 @@ def quantize_(index: GPUInvertedIndex, weight_dtype: str, keep_fp32: bool = True
     index.weights_q, index.term_scale, index.weight_dtype = q, scale, weight_dtype
     if not keep_fp32:
         index.scores = None
+    index.head_rows = None          # rebuilt in the new weight dtype on next use
     index._view = None
 
 
@@ -153,8 +165,45 @@ def ensure_blocks(index: GPUInvertedIndex) -> None:
     index.block_docs = bd
 
 
+def ensure_head(index: GPUInvertedIndex, n_head: int = N_HEAD, head_ids=None) -> None:
+    """Build the dense head rows if missing: by default the n_head terms with the longest
+    lists; doc-range shards of one corpus pass the same explicit `head_ids` so that every
+    shard sums each document's terms in the same order."""
+    if getattr(index, "head_rows", None) is not None and head_ids is None:
+        return
+    dev = index.device
+    V = int(index.vocab_size)
+    bd = getattr(index, "block_docs", None) or BLOCK_DOCS
+    ld = ((int(index.num_docs) + bd - 1) // bd) * bd
+    H = min(int(n_head), V)
+    lengths = index.lengths
+    H = min(H, int((lengths > 0).sum().item()))
+    wd = getattr(index, "weight_dtype", "fp32")
+    w, code, dt = {"fp32": (index.scores, L.W_F32, torch.float32),
+                   "bf16": (getattr(index, "weights_q", None), L.W_BF16, torch.bfloat16),
+                   "u8": (getattr(index, "weights_q", None), L.W_U8, torch.uint8)}[wd]
+    with torch.cuda.device(dev):
+        if head_ids is not None:
+            ids = torch.as_tensor(head_ids, dtype=torch.int64).to(dev).unique().to(torch.int32)
+            H = int(ids.numel())
+        elif H > 0:
+            # longest lists first, ties to the lower term id (deterministic), then id order
+            top = torch.sort(-lengths.long(), stable=True).indices[:H]
+            ids = top.sort().values.to(torch.int32).contiguous()
+        else:
+            ids = torch.zeros(0, dtype=torch.int32, device=dev)
+        slot = torch.full((V,), -1, dtype=torch.int32, device=dev)
+        slot[ids.long()] = torch.arange(H, dtype=torch.int32, device=dev)
+        rows = torch.zeros((max(H, 1), max(ld, 1)), dtype=dt, device=dev)
+        L.check(L.lib().gsp_index_head_rows(H, L.ptr(ids), L.ptr(index.offsets), L.ptr(lengths),
+                                            L.ptr(index.doc_ids), L.ptr(w), code, ld, L.ptr(rows),
+                                            L.stream_of(dev)), "head rows")
+    index.head_ids, index.head_slot, index.head_rows, index.head_ld = ids, slot, rows, ld
+
+
 def view(index: GPUInvertedIndex) -> L.IndexView:
     ensure_blocks(index)
+    ensure_head(index)
     wd = getattr(index, "weight_dtype", "fp32")
     if wd == "fp32":
         w, code = index.scores, L.W_F32
@@ -175,6 +224,10 @@ def view(index: GPUInvertedIndex) -> L.IndexView:
     v.offsets = index.offsets.data_ptr()
     v.lengths = index.lengths.data_ptr()
     v.block_starts = index.block_starts.data_ptr()
+    v.n_head = int(index.head_ids.numel())
+    v.head_slot = index.head_slot.data_ptr()
+    v.head_rows = index.head_rows.data_ptr()
+    v.head_ld = int(index.head_ld)
     return v
 
 
@@ -258,7 +311,8 @@ def index_memory_stats(index: GPUInvertedIndex) -> dict:
     doc_ids_bytes = nbytes(index.doc_ids)
     scores_bytes = nbytes(index.scores) + nbytes(index.weights_q) + nbytes(index.term_scale)
     meta_bytes = (nbytes(index.offsets) + nbytes(index.lengths) + nbytes(index.padded_lengths)
-                  + nbytes(index.max_scores) + nbytes(index.block_starts))
+                  + nbytes(index.max_scores) + nbytes(index.block_starts)
+                  + nbytes(getattr(index, "head_rows", None)))
     n = int(index.lengths.sum().item())
     npad = int(index.padded_lengths.sum().item()) if index.padded_lengths is not None else n
     return {"doc_ids_MB": doc_ids_bytes / 1e6, "scores_MB": scores_bytes / 1e6,

@@ -140,11 +140,11 @@ def shard_range(num_docs: int, world: int, rank: int):
 
 def synth_index(num_docs: int, V: int = 30522, seed: int = 0, law: Law | None = None,
                 doc_range=None, device=None, weight_dtype: str = "fp32",
-                keep_fp32: bool = True) -> GPUInvertedIndex:
+                keep_fp32: bool = True, head_ids=None) -> GPUInvertedIndex:
     """Index of documents [lo, hi) of the seeded corpus (local ids, doc_base = lo)."""
     lo, hi = doc_range if doc_range is not None else (0, num_docs)
     ip, ix, dt = synth_csr(hi - lo, V, seed, kind=0, first=lo, law=law or DOC_LAW, device=device)
     idx = build_from_csr_tensors(ip, ix, dt, V, ip.device, weight_dtype=weight_dtype, doc_base=lo,
-                                 keep_fp32=keep_fp32)
+                                 keep_fp32=keep_fp32, head_ids=head_ids)
     del ip, ix, dt
     return idx

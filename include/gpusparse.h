@@ -94,6 +94,13 @@ int gsp_index_fill(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t*
 int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t* offsets,
                        const int32_t* padded, const float* max_scores, const float* weights,
                        int32_t wdtype, void* out_weights, float* term_scale, void* stream);
+/* Dense rows of H "head" terms (no reference counterpart: a scorer-side copy of the
+ * densest posting lists).  rows [H, ld] (caller zero-filled, dtype = wdtype): row h holds
+ * the weight of term head_ids[h] in every document, 0 where the term is absent; ld is a
+ * multiple of block_docs >= n_docs. */
+int gsp_index_head_rows(int32_t H, const int32_t* head_ids, const int64_t* offsets,
+                        const int32_t* lengths, const int32_t* doc_ids, const void* weights,
+                        int32_t wdtype, int64_t ld, void* rows, void* stream);
 /* Counts posting lists that are not ascending in doc id (writes *n_bad on the host). */
 int gsp_check_sorted(int32_t V, const int32_t* doc_ids, const int64_t* offsets,
                      const int32_t* lengths, int64_t* n_bad, void* stream);
@@ -120,6 +127,12 @@ typedef struct gsp_index_view {
     const int64_t* offsets;
     const int32_t* lengths;
     const uint32_t* block_starts;
+    /* head terms scored from dense rows instead of their posting lists (n_head may be 0) */
+    int32_t n_head;
+    int32_t pad2_;
+    const int32_t* head_slot;  /* [V]: row of term t in head_rows, or -1 */
+    const void* head_rows;     /* [n_head, head_ld], weight dtype */
+    int64_t head_ld;
 } gsp_index_view;
 
 /* Workspace bytes for gsp_score_topk with this batch shape (a negative status on error). */

@@ -24,10 +24,11 @@
  *                      (torch.topk over the dense [B, N] matrix).  The reference's
  *                      summation order is unspecified (global atomics), so the oracle
  *                      fixes the canonical order the CUDA path also uses: a query's
- *                      (term id, slot) pairs in ascending order, each contribution
- *                      computed as fl(q_w * d_w) and added with one fp32 rounding
- *                      (no fused multiply-add: build with -ffp-contract=off).  Ties in
- *                      top-k are broken by ascending doc id.
+ *                      (term id, slot) pairs in ascending order, the terms of an
+ *                      optional "head" set (the index's densest terms) before all
+ *                      others, each contribution computed as fl(q_w * d_w) and added
+ *                      with one fp32 rounding (no fused multiply-add: build with
+ *                      -ffp-contract=off).  Ties in top-k are broken by ascending doc id.
  *   4. orc_score_dense_f64 - the exhaustive dense reference (src/remeasure_2026_09.py:
  *                      238-258, Q @ D^T) evaluated in fp64 for tolerance checks.
  */
@@ -210,10 +211,11 @@ int orc_build_fill(int64_t N, int32_t V, const int64_t* indptr, const int32_t* i
 
 /* ------------------------------------------------------------------ 3. scoring */
 
-typedef struct { int32_t t; int32_t slot; float w; } qent;
+typedef struct { int32_t tail; int32_t t; int32_t slot; float w; } qent;
 
 static int qent_cmp(const void* a, const void* b) {
     const qent* x = (const qent*)a; const qent* y = (const qent*)b;
+    if (x->tail != y->tail) return x->tail < y->tail ? -1 : 1;
     if (x->t != y->t) return x->t < y->t ? -1 : 1;
     return x->slot < y->slot ? -1 : (x->slot > y->slot);
 }
@@ -274,6 +276,7 @@ typedef struct {
     int64_t N; int32_t V; const int32_t* doc_ids; const float* w; const int64_t* offsets;
     const int32_t* lengths; int64_t W; const int32_t* qi; const float* qs; int64_t k;
     int64_t b0, b1; float* out_s; int64_t* out_i; float* out_acc; int64_t id_base;
+    const uint8_t* head;   /* [V] 1 for head terms, or NULL */
 } score_job;
 
 /* acc += fl(qw * w) over the query's postings in canonical (term, slot) order */
@@ -283,6 +286,7 @@ static void score_one(const score_job* j, int64_t b, float* acc, qent* ents) {
     for (int64_t s = 0; s < j->W; ++s) {
         int32_t t = j->qi[b * j->W + s];
         if (t < 0 || t >= j->V) continue;           /* triton_kernel.py:126-128 */
+        ents[ne].tail = (j->head && j->head[t]) ? 0 : 1;
         ents[ne].t = t; ents[ne].slot = (int32_t)s; ents[ne].w = j->qs[b * j->W + s]; ++ne;
     }
     qsort(ents, (size_t)ne, sizeof(qent), qent_cmp);
@@ -334,19 +338,20 @@ static int run_score(score_job base, int64_t B, int32_t nthreads) {
 int orc_score_topk(int64_t N, int32_t V, const int32_t* doc_ids, const float* weights,
                    const int64_t* offsets, const int32_t* lengths, int64_t B, int64_t W,
                    const int32_t* qi, const float* qs, int64_t k, int64_t id_base,
-                   int32_t nthreads, float* out_scores, int64_t* out_ids) {
+                   int32_t nthreads, float* out_scores, int64_t* out_ids, const uint8_t* head) {
     if (k > N) k = N;
     score_job j = {N, V, doc_ids, weights, offsets, lengths, W, qi, qs, k, 0, 0,
-                   out_scores, out_ids, NULL, id_base};
+                   out_scores, out_ids, NULL, id_base, head};
     return run_score(j, B, nthreads);
 }
 
 /* The full [B, N] fp32 score matrix in the canonical order (small cases only). */
 int orc_score_full(int64_t N, int32_t V, const int32_t* doc_ids, const float* weights,
                    const int64_t* offsets, const int32_t* lengths, int64_t B, int64_t W,
-                   const int32_t* qi, const float* qs, int32_t nthreads, float* out_acc) {
+                   const int32_t* qi, const float* qs, int32_t nthreads, float* out_acc,
+                   const uint8_t* head) {
     score_job j = {N, V, doc_ids, weights, offsets, lengths, W, qi, qs, 0, 0, 0,
-                   NULL, NULL, out_acc, 0};
+                   NULL, NULL, out_acc, 0, head};
     return run_score(j, B, nthreads);
 }
 

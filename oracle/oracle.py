@@ -59,8 +59,8 @@ def lib():
         L.orc_synth_fill.argtypes = [u64, u32, u64, i64, i32, p, p, p, p, p, p, i32]
         L.orc_build_lengths.argtypes = [i64, i32, p, p]
         L.orc_build_fill.argtypes = [i64, i32, p, p, p, p, p, p, p]
-        L.orc_score_topk.argtypes = [i64, i32, p, p, p, p, i64, i64, p, p, i64, i64, i32, p, p]
-        L.orc_score_full.argtypes = [i64, i32, p, p, p, p, i64, i64, p, p, i32, p]
+        L.orc_score_topk.argtypes = [i64, i32, p, p, p, p, i64, i64, p, p, i64, i64, i32, p, p, p]
+        L.orc_score_full.argtypes = [i64, i32, p, p, p, p, i64, i64, p, p, i32, p, p]
         L.orc_score_dense_f64.argtypes = [i64, i32, p, p, p, i64, i64, p, p, p]
         for f in ("orc_synth_nnz", "orc_synth_fill", "orc_build_lengths", "orc_build_fill",
                   "orc_score_topk", "orc_score_full", "orc_score_dense_f64"):
@@ -288,9 +288,18 @@ def topk_rows(S: np.ndarray, k: int, id_base: int = 0):
     return vals.astype(np.float32), idx + id_base
 
 
+def _head_mask(V: int, head):
+    if head is None:
+        return None
+    m = np.zeros(V, dtype=np.uint8)
+    m[np.asarray(head, dtype=np.int64)] = 1
+    return m
+
+
 def score_topk(index: Index, qi: np.ndarray, qs: np.ndarray, k: int, weights=None,
-               id_base: int = 0, nthreads: int | None = None):
-    """Exact top-k (fp32 scores [B,k], int64 ids [B,k]) in the canonical order."""
+               id_base: int = 0, nthreads: int | None = None, head=None):
+    """Exact top-k (fp32 scores [B,k], int64 ids [B,k]) in the canonical order; `head`
+    lists the term ids summed first (the scorer's dense head rows)."""
     L = lib()
     qi = np.ascontiguousarray(qi, dtype=np.int32)
     qs = np.ascontiguousarray(qs, dtype=np.float32)
@@ -300,15 +309,17 @@ def score_topk(index: Index, qi: np.ndarray, qs: np.ndarray, k: int, weights=Non
     w = np.ascontiguousarray(index.scores if weights is None else weights, dtype=np.float32)
     out_s = np.zeros((B, kk), dtype=np.float32)
     out_i = np.zeros((B, kk), dtype=np.int64)
+    hm = _head_mask(int(index.vocab_size), head)
     rc = L.orc_score_topk(N, int(index.vocab_size), _p(index.doc_ids), _p(w), _p(index.offsets),
                           _p(index.lengths), B, W, _p(qi), _p(qs), kk, id_base,
-                          nthreads or nthreads_default(), _p(out_s), _p(out_i))
+                          nthreads or nthreads_default(), _p(out_s), _p(out_i),
+                          _p(hm) if hm is not None else None)
     assert rc == 0
     return out_s, out_i
 
 
 def score_full(index: Index, qi: np.ndarray, qs: np.ndarray, weights=None,
-               nthreads: int | None = None) -> np.ndarray:
+               nthreads: int | None = None, head=None) -> np.ndarray:
     """The whole fp32 [B, N] score matrix in the canonical order."""
     L = lib()
     qi = np.ascontiguousarray(qi, dtype=np.int32)
@@ -317,9 +328,10 @@ def score_full(index: Index, qi: np.ndarray, qs: np.ndarray, weights=None,
     N = int(index.num_docs)
     w = np.ascontiguousarray(index.scores if weights is None else weights, dtype=np.float32)
     out = np.zeros((B, N), dtype=np.float32)
+    hm = _head_mask(int(index.vocab_size), head)
     rc = L.orc_score_full(N, int(index.vocab_size), _p(index.doc_ids), _p(w), _p(index.offsets),
                           _p(index.lengths), B, W, _p(qi), _p(qs), nthreads or nthreads_default(),
-                          _p(out))
+                          _p(out), _p(hm) if hm is not None else None)
     assert rc == 0
     return out
 

@@ -71,7 +71,7 @@ def test_reference_style_index_without_blocks():
     idx.num_docs, idx.vocab_size, idx.device = 3000, 30522, DEV
     qi, qs = O.synth_queries(16, 30522, seed=15)
     s, i = gpusparse.triton_fused_score(idx, t(qi), t(qs), top_k=200)
-    rs, ri = O.score_topk(ref, qi, qs, 200)
+    rs, ri = O.score_topk(ref, qi, qs, 200, head=idx.head_ids.cpu().numpy())
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
 
 
@@ -128,7 +128,7 @@ def test_plugin_retrieve_chunked_path_and_run_file(tmp_path):
     chunk = P.retrieve(idx, qids, ti, ts, dids, k=100, batch_size=7, doc_chunk=512)
     assert mono == chunk
     oidx = O.build_index(ip, ix, dt, dim)
-    rs, ri = O.score_topk(oidx, qi, qs, 100)
+    rs, ri = O.score_topk(oidx, qi, qs, 100, head=idx.head_ids.cpu().numpy())
     for b in range(30):
         exp = [(f"q{b}", float(s), f"d{d}") for s, d in zip(rs[b], ri[b]) if s > 0]
         assert mono[b] == exp

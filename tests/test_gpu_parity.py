@@ -24,6 +24,11 @@ def t(a):
     return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
 
 
+def hd(g):
+    """The GPU index's head terms: the oracle sums them first, as the scorer does."""
+    return g.head_ids.cpu().numpy()
+
+
 @pytest.fixture(scope="module")
 def corpus():
     ip, ix, dt = O.synth_csr(20000, V, seed=0)
@@ -43,7 +48,7 @@ def test_fp32_bit_exact(corpus, gindex, k):
     _, _, _, oidx = corpus
     qi, qs = O.synth_queries(96, V, seed=1)
     s, i = gpusparse.triton_fused_score(gindex, t(qi), t(qs), top_k=k)
-    rs, ri = O.score_topk(oidx, qi, qs, k)
+    rs, ri = O.score_topk(oidx, qi, qs, k, head=hd(gindex))
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
 
 
@@ -79,7 +84,7 @@ def test_edge_queries(corpus, gindex):
     qi[5, :2] = [29_000, 30_000]; qs[5, :2] = [1.0, 1.0]                   # rare terms
     for k in (10, 1000):
         s, i = gpusparse.triton_fused_score(gindex, t(qi), t(qs), top_k=k)
-        rs, ri = O.score_topk(oidx, qi, qs, k)
+        rs, ri = O.score_topk(oidx, qi, qs, k, head=hd(gindex))
         assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
     assert np.array_equal(i.cpu().numpy()[2], np.arange(1000))
 
@@ -92,7 +97,7 @@ def test_int64_query_ids_are_accepted(corpus, gindex):
     qi64[0, -1] = 2 ** 40                      # out of range, must be skipped not wrapped
     s, i = gpusparse.triton_fused_score(gindex, t(qi64), t(qs), top_k=50)
     qi[0, -1] = -1
-    rs, ri = O.score_topk(oidx, qi, qs, 50)
+    rs, ri = O.score_topk(oidx, qi, qs, 50, head=hd(gindex))
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
 
 
@@ -104,7 +109,7 @@ def test_small_corpora_k_at_least_n(N, k):
     g = gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), V, DEV)
     qi, qs = O.synth_queries(40, V, seed=2)
     s, i = gpusparse.triton_fused_score(g, t(qi), t(qs), top_k=k)
-    rs, ri = O.score_topk(oidx, qi, qs, k)
+    rs, ri = O.score_topk(oidx, qi, qs, k, head=hd(g))
     assert s.shape == (40, min(k, N))
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
 
@@ -115,7 +120,7 @@ def test_batch_sizes(corpus, gindex, B):
     _, _, _, oidx = corpus
     qi, qs = O.synth_queries(B, V, seed=10 + B)
     s, i = gpusparse.triton_fused_score(gindex, t(qi), t(qs), top_k=100)
-    rs, ri = O.score_topk(oidx, qi, qs, 100)
+    rs, ri = O.score_topk(oidx, qi, qs, 100, head=hd(gindex))
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
 
 
@@ -129,7 +134,7 @@ def test_wide_queries():
     qi = rng.integers(0, 2000, size=(10, 700)).astype(np.int32)
     qs = rng.random((10, 700)).astype(np.float32)
     s, i = gpusparse.triton_fused_score(g, t(qi), t(qs), top_k=300)
-    rs, ri = O.score_topk(oidx, qi, qs, 300)
+    rs, ri = O.score_topk(oidx, qi, qs, 300, head=hd(g))
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
 
 
@@ -143,7 +148,7 @@ def test_quantised_modes_bit_exact_vs_dequantised_oracle(corpus, wd):
     w = gpusparse.dequantized_weights(g).cpu().numpy()
     qi, qs = O.synth_queries(64, V, seed=8)
     s, i = gpusparse.triton_fused_score(g, t(qi), t(qs), top_k=1000)
-    rs, ri = O.score_topk(oidx, qi, qs, 1000, weights=w)
+    rs, ri = O.score_topk(oidx, qi, qs, 1000, weights=w, head=hd(g))
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
 
 
@@ -179,16 +184,19 @@ def test_shards_merge_equals_unsharded(corpus):
     N = len(ip) - 1
     qi, qs = O.synth_queries(50, V, seed=9)
     k = 1000
+    full = gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), V, DEV)
+    head = hd(full)        # one head set for every shard: the same summation order
     for world in (2, 3, 8):
         keys = []
         for r in range(world):
             lay = ShardLayout(N, world, r)
             sip = ip[lay.lo:lay.hi + 1] - ip[lay.lo]
             g = gpusparse.build_from_csr_tensors(t(sip), t(ix[ip[lay.lo]:ip[lay.hi]]),
-                                                 t(dt[ip[lay.lo]:ip[lay.hi]]), V, DEV, doc_base=lay.lo)
+                                                 t(dt[ip[lay.lo]:ip[lay.hi]]), V, DEV, doc_base=lay.lo,
+                                                 head_ids=head)
             _, _, kk = gpusparse.score_topk(g, t(qi), t(qs), k, with_keys=True)
             keys.append(kk)
         allk = torch.stack(keys)
         s, i = gpusparse.merge_topk(allk, ShardLayout(N, world, 0).list_counts(k), k)
-        rs, ri = O.score_topk(oidx, qi, qs, k)
+        rs, ri = O.score_topk(oidx, qi, qs, k, head=head)
         assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
