@@ -155,6 +155,7 @@ __global__ void quant_kernel(int32_t V, const int64_t* __restrict__ offsets,
   }
 }
 
+// n_bad[0]: lists with a descending step; n_bad[1]: lists that repeat a doc id.
 __global__ void check_sorted_kernel(int32_t V, const int32_t* __restrict__ doc_ids,
                                     const int64_t* __restrict__ offsets,
                                     const int32_t* __restrict__ lengths,
@@ -164,9 +165,14 @@ __global__ void check_sorted_kernel(int32_t V, const int32_t* __restrict__ doc_i
   if (t >= V) return;
   const int64_t o = offsets[t];
   const int32_t L = lengths[t];
-  bool bad = false;
-  for (int32_t p = lane + 1; p < L; p += 32) bad |= doc_ids[o + p] < doc_ids[o + p - 1];
+  bool bad = false, dup = false;
+  for (int32_t p = lane + 1; p < L; p += 32) {
+    const int32_t a = doc_ids[o + p - 1], b = doc_ids[o + p];
+    bad |= b < a;
+    dup |= b == a;
+  }
   if (__any_sync(FULL, bad) && lane == 0) atomicAdd(n_bad, 1ull);
+  if (__any_sync(FULL, dup) && lane == 0) atomicAdd(n_bad + 1, 1ull);
 }
 
 // out[c][t] = offsets[t] + #postings of t with doc id < min(c*chunk, n_docs); one warp per
@@ -292,8 +298,6 @@ extern "C" int gsp_index_fill(int64_t n_docs, int32_t V, int32_t block_docs, con
                               float* max_scores, void* ws, int64_t ws_bytes, void* stream) {
   int rc = check_csr_args(n_docs, V, block_docs, indptr);
   if (rc) return rc;
-  (void)ws;
-  (void)ws_bytes;
   cudaStream_t st = as_stream(stream);
   const int64_t nb = n_blocks_of(n_docs, block_docs);
   if (total_padded > 0) {
@@ -312,6 +316,20 @@ extern "C" int gsp_index_fill(int64_t n_docs, int32_t V, int32_t block_docs, con
   max_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, st>>>(V, offsets, lengths, weights,
                                                                        max_scores);
   GSP_CHECK_LAUNCH();
+  // a term listed twice in one document row would give one list a repeated doc id; the
+  // scorer applies a list's postings to distinct documents in parallel, so that is refused
+  GSP_REQUIRE(ws && ws_bytes >= 16, GSP_ERR_ARG, "gsp_index_fill: workspace too small");
+  unsigned long long* d_cnt = static_cast<unsigned long long*>(ws);
+  GSP_CUDA(cudaMemsetAsync(d_cnt, 0, 16, st));
+  check_sorted_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, st>>>(V, doc_ids, offsets,
+                                                                                 lengths, d_cnt);
+  GSP_CHECK_LAUNCH();
+  unsigned long long h[2] = {0, 0};
+  GSP_CUDA(cudaMemcpyAsync(h, d_cnt, 16, cudaMemcpyDeviceToHost, st));
+  GSP_CUDA(cudaStreamSynchronize(st));
+  GSP_REQUIRE(h[1] == 0, GSP_ERR_UNSORTED,
+              "index build: %llu terms occur twice in one document row (duplicate (doc, term) "
+              "entries); merge them first, e.g. scipy's csr_matrix.sum_duplicates()", h[1]);
   return GSP_OK;
 }
 
@@ -329,21 +347,22 @@ extern "C" int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t
 }
 
 extern "C" int gsp_check_sorted(int32_t V, const int32_t* doc_ids, const int64_t* offsets,
-                                const int32_t* lengths, int64_t* n_bad, void* stream) {
+                                const int32_t* lengths, int64_t* n_bad, int64_t* n_dup, void* stream) {
   GSP_REQUIRE(V > 0 && doc_ids && offsets && lengths && n_bad, GSP_ERR_ARG,
               "gsp_check_sorted: bad arguments");
   cudaStream_t st = as_stream(stream);
   unsigned long long* d_bad = nullptr;
-  GSP_CUDA(cudaMallocAsync(&d_bad, sizeof(unsigned long long), st));
-  GSP_CUDA(cudaMemsetAsync(d_bad, 0, sizeof(unsigned long long), st));
+  GSP_CUDA(cudaMallocAsync(&d_bad, 2 * sizeof(unsigned long long), st));
+  GSP_CUDA(cudaMemsetAsync(d_bad, 0, 2 * sizeof(unsigned long long), st));
   check_sorted_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, st>>>(V, doc_ids, offsets,
                                                                                  lengths, d_bad);
   GSP_CHECK_LAUNCH();
-  unsigned long long h = 0;
-  GSP_CUDA(cudaMemcpyAsync(&h, d_bad, sizeof(h), cudaMemcpyDeviceToHost, st));
+  unsigned long long h[2] = {0, 0};
+  GSP_CUDA(cudaMemcpyAsync(h, d_bad, sizeof(h), cudaMemcpyDeviceToHost, st));
   GSP_CUDA(cudaFreeAsync(d_bad, st));
   GSP_CUDA(cudaStreamSynchronize(st));
-  *n_bad = int64_t(h);
+  *n_bad = int64_t(h[0]);
+  if (n_dup) *n_dup = int64_t(h[1]);
   return GSP_OK;
 }
 
@@ -353,7 +372,7 @@ extern "C" int gsp_chunk_bounds(int64_t n_docs, int32_t V, int64_t doc_chunk, co
   GSP_REQUIRE(n_docs >= 0 && V > 0 && doc_chunk > 0 && out, GSP_ERR_ARG,
               "gsp_chunk_bounds: bad arguments");
   int64_t n_bad = 0;
-  int rc = gsp_check_sorted(V, doc_ids, offsets, lengths, &n_bad, stream);
+  int rc = gsp_check_sorted(V, doc_ids, offsets, lengths, &n_bad, nullptr, stream);
   if (rc) return rc;
   GSP_REQUIRE(n_bad == 0, GSP_ERR_UNSORTED,
               "%lld posting lists are not ascending in doc_id. Chunked scoring requires "

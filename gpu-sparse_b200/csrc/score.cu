@@ -19,7 +19,7 @@
 // Per tile:
 //  1. head terms (the index's densest terms, stored as dense rows): the warp keeps the
 //     1024 accumulators in registers (32 per lane) and streams each head row of the query
-//     with coalesced vector loads: acc += fl(q_w * w) for every document;
+//     with coalesced vector loads: acc = fma(q_w, w, acc) for every document;
 //  2. the accumulators go to shared memory and the tail terms (all others), in ascending
 //     term id, are scattered into them: a run whose window is long (or that a query
 //     repeats) is streamed on its own, four 32-posting chunks in flight; consecutive short
@@ -32,9 +32,10 @@
 //     threshold, which it also publishes (atomicMax) as a lower bound for the query's
 //     other streams.  A discarded key is beaten by k kept keys, so the final top-k
 //     (merge_kernel in select.cu) is exact.
-// Each cell therefore sums fl(q_w * d_w) in a fixed order -- head terms by term id, then
-// tail terms by term id, a repeated term in query-slot order -- with one fp32 rounding per
-// product and per sum: bitwise reproducible, and equal to the CPU oracle's canonical order.
+// Each cell therefore accumulates acc = fma(q_w, d_w, acc) in a fixed order -- head terms
+// by term id, then tail terms by term id, a repeated term in query-slot order -- with one
+// fp32 rounding per fused multiply-add: bitwise reproducible, and equal to the CPU
+// oracle's canonical order.
 #include "common.cuh"
 
 #include <algorithm>
@@ -47,6 +48,14 @@
 namespace gsp {
 
 constexpr int kWarps = 8;
+#ifndef GSP_SCORE_CTAS_PER_SM
+#define GSP_SCORE_CTAS_PER_SM 4   // resident scoring CTAs per SM (register budget 65536 / (256 * this))
+#endif
+constexpr int kCtasPerSm = GSP_SCORE_CTAS_PER_SM;
+// with four CTAs per SM (64 registers) the head rows are summed in two halves of the tile,
+// with five or more in quarters, holding fewer accumulators and row values in registers
+constexpr int kHeadParts = kCtasPerSm >= 5 ? 4 : (kCtasPerSm >= 4 ? 2 : 1);
+constexpr int kHeadVec = 1024 / 128 / kHeadParts;   // float4 accumulators per lane per part
 constexpr int kPlanThreads = 256;
 constexpr int kMaxWidth = 4096;   // query slots (W) supported
 constexpr int kTile = 1024;       // documents per tile = index block
@@ -343,13 +352,13 @@ __device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t 
   return prefix;
 }
 
-// acc[col] += fl(qw * w); the column test keeps a list that breaks the ascending-doc-id
-// invariant from ever addressing outside the tile.
+// acc[col] = fma(qw, w, acc[col]); the column test keeps a list that breaks the
+// ascending-doc-id invariant from ever addressing outside the tile.
 __device__ __forceinline__ void acc_add(float* __restrict__ acc, int32_t col, uint32_t span, float qw,
                                         float w) {
   if (uint32_t(col) < span) {
     float* a = acc + col;
-    *a = __fadd_rn(*a, __fmul_rn(qw, w));
+    *a = __fmaf_rn(qw, w, *a);
   }
 }
 
@@ -358,7 +367,9 @@ constexpr int kUnroll = 4;   // posting chunks of one run in flight together
 // Postings [0, n) of one run (pd/pw point at its window) applied to its NE entries (NE = 1
 // or 2 in registers; NE = 0: ne entries read from ew).  Every pass issues the loads of
 // kUnroll chunks (predicated past n) before it applies any, so a run costs one memory
-// round trip per 32 * kUnroll postings.
+// round trip per 32 * kUnroll postings.  A list holds each document at most once (the
+// index build refuses repeats), so the pass reads all its accumulators, updates them in
+// registers and writes them back without ordering the shared-memory accesses.
 template <typename WT, int NE>
 __device__ __forceinline__ void run_window(const int32_t* __restrict__ pd, const WT* __restrict__ pw,
                                            float scale, int32_t n, int32_t d0i, uint32_t span,
@@ -367,7 +378,7 @@ __device__ __forceinline__ void run_window(const int32_t* __restrict__ pd, const
   const int lane = lane_id();
   for (int32_t base = 0; base < n; base += 32 * kUnroll) {
     int32_t col[kUnroll];
-    float w[kUnroll];
+    float w[kUnroll], v[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const int32_t i = base + 32 * u + lane;
@@ -379,12 +390,18 @@ __device__ __forceinline__ void run_window(const int32_t* __restrict__ pd, const
       }
     }
 #pragma unroll
+    for (int u = 0; u < kUnroll; ++u) v[u] = uint32_t(col[u]) < span ? acc[col[u]] : 0.f;
+#pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      if constexpr (NE >= 1) acc_add(acc, col[u], span, w_a, w[u]);
-      if constexpr (NE >= 2) acc_add(acc, col[u], span, w_b, w[u]);
+      if constexpr (NE >= 1) v[u] = __fmaf_rn(w_a, w[u], v[u]);
+      if constexpr (NE >= 2) v[u] = __fmaf_rn(w_b, w[u], v[u]);
       if constexpr (NE == 0) {
-        for (int32_t e = 0; e < ne; ++e) acc_add(acc, col[u], span, ew[e], w[u]);
+        for (int32_t e = 0; e < ne; ++e) v[u] = __fmaf_rn(ew[e], w[u], v[u]);
       }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (uint32_t(col[u]) < span) acc[col[u]] = v[u];
     }
   }
 }
@@ -416,14 +433,44 @@ struct Vec4<uint8_t> {
 };
 
 __device__ __forceinline__ void fma4(float4& a, float qw, const float4 v) {
-  a.x = __fadd_rn(a.x, __fmul_rn(qw, v.x));
-  a.y = __fadd_rn(a.y, __fmul_rn(qw, v.y));
-  a.z = __fadd_rn(a.z, __fmul_rn(qw, v.z));
-  a.w = __fadd_rn(a.w, __fmul_rn(qw, v.w));
+  a.x = __fmaf_rn(qw, v.x, a.x);
+  a.y = __fmaf_rn(qw, v.y, a.y);
+  a.z = __fmaf_rn(qw, v.z, a.z);
+  a.w = __fmaf_rn(qw, v.w, a.w);
+}
+
+// Bit 4 * i + j of the result: document 128 * i + 4 * lane + j of the tile (below span)
+// has a score at or above the score of threshold key thr.
+__device__ __forceinline__ uint32_t mark_tile(const float* __restrict__ acc, int lane, uint32_t span,
+                                              uint64_t thr) {
+  const uint32_t thi = uint32_t(thr >> 32);
+  const float ts = thi < 0x00800000u ? -INFINITY : fkey_inv(thi);
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < kTile / 128; ++i) {
+    const float4 v = *reinterpret_cast<const float4*>(acc + 128 * i + 4 * lane);
+    const uint32_t c = uint32_t(128 * i + 4 * lane);
+    m |= uint32_t(c < span && v.x >= ts) << (4 * i);
+    m |= uint32_t(c + 1 < span && v.y >= ts) << (4 * i + 1);
+    m |= uint32_t(c + 2 < span && v.z >= ts) << (4 * i + 2);
+    m |= uint32_t(c + 3 < span && v.w >= ts) << (4 * i + 3);
+  }
+  return m;
+}
+
+// Inclusive warp prefix sum.
+__device__ __forceinline__ int32_t lane_scan(int32_t x) {
+  const int lane = lane_id();
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(FULL, x, o);
+    if (lane >= o) x += y;
+  }
+  return x;
 }
 
 template <typename WT>
-__global__ void __launch_bounds__(kWarps * 32, 3)
+__global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 score_kernel(const ScoreParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int lane = lane_id(), wid = threadIdx.x >> 5;
@@ -508,25 +555,31 @@ score_kernel(const ScoreParams p) {
       const int32_t d1 = int32_t(min64(int64_t(b + 1) * kTile, p.n_docs));
       const uint32_t span = uint32_t(d1 - d0i);
 
-      // 1. head rows, accumulators in registers: lane owns documents 128*i + 4*lane + j
-      float4 a[kTile / 128];
+      // 1. head rows, accumulators in registers: in each of the kHeadParts parts of the
+      // tile, lane owns documents part * kTile / kHeadParts + 128 * i + 4 * lane + j
+#pragma unroll 1
+      for (int part = 0; part < kHeadParts; ++part) {
+        const int32_t pofs = part * (kTile / kHeadParts);
+        float4 a[kHeadVec];
 #pragma unroll
-      for (int i = 0; i < kTile / 128; ++i) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int32_t e = 0; e < nhe; ++e) {
-        const int32_t h = head_h[e];
-        const float qw = head_w[e];
-        float sc = 1.0f;
-        if constexpr (std::is_same<WT, uint8_t>::value) sc = head_sc[e];
-        const WT* row = hrows + int64_t(h) * p.head_ld + d0i + 4 * lane;
-        float4 v[kTile / 128];
+        for (int i = 0; i < kHeadVec; ++i) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int32_t e = 0; e < nhe; ++e) {
+          const int32_t h = head_h[e];
+          const float qw = head_w[e];
+          float sc = 1.0f;
+          if constexpr (std::is_same<WT, uint8_t>::value) sc = head_sc[e];
+          const WT* row = hrows + int64_t(h) * p.head_ld + d0i + pofs + 4 * lane;
+          float4 v[kHeadVec];
 #pragma unroll
-        for (int i = 0; i < kTile / 128; ++i) v[i] = Vec4<WT>::get(row + 128 * i, sc);
+          for (int i = 0; i < kHeadVec; ++i) v[i] = Vec4<WT>::get(row + 128 * i, sc);
 #pragma unroll
-        for (int i = 0; i < kTile / 128; ++i) fma4(a[i], qw, v[i]);
+          for (int i = 0; i < kHeadVec; ++i) fma4(a[i], qw, v[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < kHeadVec; ++i) *reinterpret_cast<float4*>(acc + pofs + 128 * i + 4 * lane) = a[i];
       }
-#pragma unroll
-      for (int i = 0; i < kTile / 128; ++i) *reinterpret_cast<float4*>(acc + 128 * i + 4 * lane) = a[i];
       __syncwarp();
+      const unsigned long long g_pub = __ldcg(p.gthr + q);   // consumed by the selection
 
       // 2. tail runs in ascending term id
       const uint32_t* __restrict__ brow = p.block_starts + int64_t(b) * p.V;
@@ -623,30 +676,37 @@ score_kernel(const ScoreParams p) {
       }
       __syncwarp();
 
-      // 3. fused selection (a float comparison rejects almost every document first)
-      thr = max(thr, uint64_t(__ldcg(p.gthr + q)));
-      const uint32_t thi = uint32_t(thr >> 32);
-      const float thr_s = thi < 0x00800000u ? -INFINITY : fkey_inv(thi);
-      for (int32_t c0 = 0; c0 < int32_t(span); c0 += 32) {
-        const int32_t col = c0 + lane;
-        const bool valid = col < int32_t(span);
-        const float s = acc[valid ? col : 0];
-        if (!__ballot_sync(FULL, valid && s >= thr_s)) continue;
-        const uint64_t key = pack_key(s, uint32_t(p.doc_base + d0i + col));
-        bool pass = valid && key >= thr;
-        uint32_t bal = __ballot_sync(FULL, pass);
-        if (!bal) continue;
-        if (nbuf + __popc(bal) > p.C) {
+      // 3. fused selection.  Every lane reads its 32 accumulators (documents 128 * i +
+      // 4 * lane + j) with vector loads and marks those whose score reaches the threshold's
+      // score; the marked documents' keys are appended to the buffer at per-lane offsets
+      // (a superset of the keys >= thr is harmless: only the k largest survive).  The
+      // buffer holds at least k + kTile keys, so after a compaction a tile always fits.
+      thr = max(thr, uint64_t(g_pub));
+      uint32_t m = mark_tile(acc, lane, span, thr);
+      int32_t cnt = __popc(m);
+      if (__any_sync(FULL, cnt != 0)) {
+        int32_t incl = lane_scan(cnt);
+        int32_t total = __shfl_sync(FULL, incl, 31);
+        if (nbuf + total > p.C) {
           thr = warp_compact(buf, nbuf, p.k, hist);
           nbuf = p.k;
           if (lane == 0) atomicMax(p.gthr + q, (unsigned long long)thr);
-          pass = pass && key >= thr;
-          bal = __ballot_sync(FULL, pass);
+          m = mark_tile(acc, lane, span, thr);
+          cnt = __popc(m);
+          incl = lane_scan(cnt);
+          total = __shfl_sync(FULL, incl, 31);
         }
-        if (pass) buf[nbuf + __popc(bal & lanemask_lt())] = key;
-        nbuf += __popc(bal);
+        int32_t o = nbuf + incl - cnt;
+        const uint32_t dbase = uint32_t(p.doc_base + d0i);
+        while (m) {
+          const int bit = __ffs(m) - 1;
+          m &= m - 1;
+          const int32_t col = 128 * (bit >> 2) + 4 * lane + (bit & 3);
+          buf[o++] = pack_key(acc[col], dbase + uint32_t(col));
+        }
+        nbuf += total;
+        __syncwarp();
       }
-      __syncwarp();
     }
     if (nbuf > p.k) {
       const uint64_t t2 = warp_compact(buf, nbuf, p.k, hist);
@@ -710,7 +770,7 @@ int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) 
   const int sms = num_sms();
   c.ecap = W;
   c.smem = WarpLayout::total * kWarps;
-  c.ctas_per_sm = 3;
+  c.ctas_per_sm = kCtasPerSm;
   c.npow2 = kPlanThreads;
   while (c.npow2 < W) c.npow2 <<= 1;
   c.n_blocks = (ix->n_docs + kTile - 1) / kTile;
@@ -719,7 +779,9 @@ int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) 
   c.S = int(std::max<int64_t>(warps, B));
   c.H = c.S;
   c.grid = int(std::min<int64_t>(int64_t(sms) * c.ctas_per_sm, (c.S + kWarps - 1) / kWarps));
-  c.C = int(((std::max<int64_t>(2 * c.kk, c.kk + 256) + 31) / 32) * 32);
+  // room for k kept keys plus one whole tile, so a tile's candidates always fit after a
+  // compaction
+  c.C = int(((std::max<int64_t>(2 * c.kk, c.kk + kTile) + 31) / 32) * 32);
   set_layout(c, B);
   return GSP_OK;
 }

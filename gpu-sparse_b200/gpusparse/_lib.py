@@ -85,7 +85,8 @@ def lib() -> ctypes.CDLL:
                                               i64, p]),
             "gsp_index_quantize": (ctypes.c_int, [i32, i64, p, p, p, p, i32, p, p, p]),
             "gsp_index_head_rows": (ctypes.c_int, [i32, p, p, p, p, p, i32, i64, p, p]),
-            "gsp_check_sorted": (ctypes.c_int, [i32, p, p, p, ctypes.POINTER(i64), p]),
+            "gsp_check_sorted": (ctypes.c_int, [i32, p, p, p, ctypes.POINTER(i64),
+                                                ctypes.POINTER(i64), p]),
             "gsp_chunk_bounds": (ctypes.c_int, [i64, i32, i64, p, p, p, p, p]),
             "gsp_score_ws_bytes": (i64, [ctypes.POINTER(IndexView), i64, i64, i64]),
             "gsp_score_topk": (ctypes.c_int, [ctypes.POINTER(IndexView), p, p, i64, i64, i64, p,

@@ -155,11 +155,22 @@ def dequantized_weights(index: GPUInvertedIndex) -> torch.Tensor:
 
 def ensure_blocks(index: GPUInvertedIndex) -> None:
     """Derive block_starts for an index constructed without them (e.g. field by field, as
-    the reference's plug-in does); validates that lists ascend (ValueError otherwise)."""
+    the reference's plug-in does); validates that lists strictly ascend (ValueError for a
+    descending step or a repeated doc id)."""
     if getattr(index, "block_starts", None) is not None:
         return
     from .scoring import build_chunk_boundaries
     bd = getattr(index, "block_docs", None) or BLOCK_DOCS
+    dev = index.device if isinstance(index.device, torch.device) else torch.device(index.device)
+    n_bad, n_dup = ctypes.c_int64(0), ctypes.c_int64(0)
+    with torch.cuda.device(dev):
+        L.check(L.lib().gsp_check_sorted(int(index.vocab_size), L.ptr(index.doc_ids),
+                                         L.ptr(index.offsets), L.ptr(index.lengths),
+                                         ctypes.byref(n_bad), ctypes.byref(n_dup), L.stream_of(dev)),
+                "index check")
+    if n_dup.value:
+        raise ValueError(f"{n_dup.value} posting lists repeat a doc id (a term listed twice in one "
+                         "document); merge duplicate (doc, term) entries first")
     b = build_chunk_boundaries(index, bd)
     index.block_starts = (b - index.offsets.unsqueeze(0)).to(torch.int32).contiguous()
     index.block_docs = bd

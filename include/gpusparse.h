@@ -101,9 +101,13 @@ int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t* offsets,
 int gsp_index_head_rows(int32_t H, const int32_t* head_ids, const int64_t* offsets,
                         const int32_t* lengths, const int32_t* doc_ids, const void* weights,
                         int32_t wdtype, int64_t ld, void* rows, void* stream);
-/* Counts posting lists that are not ascending in doc id (writes *n_bad on the host). */
+/* Counts posting lists that are not ascending in doc id (*n_bad) and, when n_dup is not
+ * NULL, lists that repeat a doc id (*n_dup); both written on the host.  The scorer needs
+ * strictly ascending lists: gsp_index_fill refuses a CSR that lists a term twice in one
+ * row, and a caller that assembles an index itself checks n_dup == 0.
+ * Replaces the check in src/triton_kernel_chunked.py:99-108. */
 int gsp_check_sorted(int32_t V, const int32_t* doc_ids, const int64_t* offsets,
-                     const int32_t* lengths, int64_t* n_bad, void* stream);
+                     const int32_t* lengths, int64_t* n_bad, int64_t* n_dup, void* stream);
 
 /* ---------------------------------------------------------------- chunk bounds */
 /* build_chunk_boundaries: out int64 [n_chunks+1, V], out[c][t] = offsets[t] + number of

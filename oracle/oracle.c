@@ -26,12 +26,14 @@
  *                      fixes the canonical order the CUDA path also uses: a query's
  *                      (term id, slot) pairs in ascending order, the terms of an
  *                      optional "head" set (the index's densest terms) before all
- *                      others, each contribution computed as fl(q_w * d_w) and added
- *                      with one fp32 rounding (no fused multiply-add: build with
- *                      -ffp-contract=off).  Ties in top-k are broken by ascending doc id.
+ *                      others, each contribution added as acc = fma(q_w, d_w, acc):
+ *                      one fused multiply-add, a single IEEE fp32 rounding (C99 fmaf;
+ *                      nothing else may be contracted: build with -ffp-contract=off).
+ *                      Ties in top-k are broken by ascending doc id.
  *   4. orc_score_dense_f64 - the exhaustive dense reference (src/remeasure_2026_09.py:
  *                      238-258, Q @ D^T) evaluated in fp64 for tolerance checks.
  */
+#include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -279,7 +281,10 @@ typedef struct {
     const uint8_t* head;   /* [V] 1 for head terms, or NULL */
 } score_job;
 
-/* acc += fl(qw * w) over the query's postings in canonical (term, slot) order */
+/* acc = fma(qw, w, acc) over the query's postings in canonical (term, slot) order.  The
+ * FMA-capable clone is picked at load time where the CPU has the instruction; both clones
+ * compute the same correctly rounded fmaf. */
+__attribute__((target_clones("fma", "default")))
 static void score_one(const score_job* j, int64_t b, float* acc, qent* ents) {
     memset(acc, 0, sizeof(float) * (size_t)j->N);
     int64_t ne = 0;
@@ -297,8 +302,7 @@ static void score_one(const score_job* j, int64_t b, float* acc, qent* ents) {
         for (int32_t p = 0; p < L; ++p) {
             const int32_t d = j->doc_ids[o + p];
             if (d < 0) continue;                     /* padding (:156 mask) */
-            const float c = qw * j->w[o + p];        /* one rounding for the product */
-            acc[d] = acc[d] + c;                     /* one rounding for the sum */
+            acc[d] = fmaf(qw, j->w[o + p], acc[d]);  /* one rounding (fused) */
         }
     }
 }

@@ -37,11 +37,12 @@ WTAB_SEGS = 65536
 
 
 def build_lib(force: bool = False) -> str:
-    """Compile oracle.c into oracle/liboracle.so (no FMA contraction)."""
+    """Compile oracle.c into oracle/liboracle.so (no implicit FMA contraction; the scorer's
+    explicit fmaf is the canonical arithmetic)."""
     src = os.path.join(_HERE, "oracle.c")
     if force or not os.path.exists(_SO) or os.path.getmtime(_SO) < os.path.getmtime(src):
         subprocess.check_call(["gcc", "-O3", "-ffp-contract=off", "-fno-fast-math", "-fPIC",
-                               "-shared", "-pthread", src, "-o", _SO])
+                               "-shared", "-pthread", src, "-o", _SO, "-lm"])
     return _SO
 
 

@@ -137,3 +137,31 @@ def test_plugin_retrieve_chunked_path_and_run_file(tmp_path):
     lines = gzip.open(tmp_path / "run.txt.gz", "rt").read().splitlines()
     assert lines[0].split()[:4] == ["q0", "Q0", mono[0][0][2], "1"]
     assert len(lines) == sum(len(r) for r in mono)
+
+
+def test_duplicate_doc_term_entries_are_refused():
+    """A term listed twice in one CSR row would repeat a doc id inside its posting list;
+    the scorer updates a list's documents in parallel, so the build refuses it."""
+    import gpusparse
+    ip, ix, dt = O.synth_csr(50, 30522, seed=21)
+    ix = ix.copy()
+    ix[ip[3] + 1] = ix[ip[3]]                                 # doc 3 lists one term twice
+    with pytest.raises(ValueError, match="twice"):
+        gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), 30522, DEV)
+
+
+def test_reference_style_index_with_repeated_doc_is_refused():
+    import gpusparse
+    ip, ix, dt = O.synth_csr(300, 30522, seed=22)
+    ref = O.build_index(ip, ix, dt, 30522)
+    d = ref.doc_ids.copy()
+    t0 = int(np.argmax(ref.lengths))
+    o = int(ref.offsets[t0])
+    d[o + 1] = d[o]                                           # a repeated doc id in one list
+    idx = gpusparse.GPUInvertedIndex.__new__(gpusparse.GPUInvertedIndex)
+    idx.doc_ids, idx.scores = t(d), t(ref.scores)
+    idx.offsets, idx.lengths = t(ref.offsets), t(ref.lengths)
+    idx.num_docs, idx.vocab_size, idx.device = 300, 30522, DEV
+    qi, qs = O.synth_queries(4, 30522, seed=23)
+    with pytest.raises(ValueError, match="repeat"):
+        gpusparse.triton_fused_score(idx, t(qi), t(qs), top_k=10)
