@@ -46,14 +46,9 @@ int max_smem_optin();
 int merge_topk_device(const uint64_t* keys, int64_t B, int64_t R, int64_t stride_b,
                       int64_t stride_r, const int32_t* counts_dev, int64_t cstride_b,
                       const int32_t* counts_host, int64_t k, float* out_scores, int64_t* out_ids,
-                      uint64_t* out_keys, cudaStream_t st, int64_t pad_id = -1);
-// Same, with a ragged number of lists per query: the lists of query q are s in
-// [first[q], first[q+1]) and S + help_list[q * max_help + m] for m < min(help_count[q],
-// max_help), each at keys + s * stride with counts_dev[s] valid entries.
-int merge_streams_device(const uint64_t* keys, int64_t B, const int32_t* first, const int32_t* help_list,
-                         const int32_t* help_count, int32_t max_help, int32_t S, int64_t stride,
-                         const int32_t* counts_dev, int64_t k, float* out_scores, int64_t* out_ids,
-                         uint64_t* out_keys, cudaStream_t st);
+                      uint64_t* out_keys, cudaStream_t st, int64_t pad_id = -1,
+                      const int32_t* fault = nullptr);
+
 
 // ---- order-preserving float <-> uint32 key (-0 folded onto +0) ----------------------
 __host__ __device__ __forceinline__ uint32_t fkey(float f) {

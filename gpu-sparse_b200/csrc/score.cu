@@ -3,18 +3,24 @@
 // Replaces src/triton_kernel.py:93-200 (_fast_scatter_add_kernel + torch.zeros +
 // torch.topk), src/triton_kernel_chunked.py:34-170 and src/fused_topk.py:33-160.
 //
-// Work decomposition.  Every query gets J_q "streams", J_q proportional to its estimated
-// work (its tail postings and dense head rows), one stream per resident warp in total.
-// The streams of a query take its document tiles in ascending order from a per-query
-// counter, so all queries sweep the document space at about the same relative pace and
-// the tiles in flight at any moment are a narrow window whose postings stay in L2.  A
-// stream keeps one candidate buffer (and a threshold that tightens) across its sweep.  A
-// warp whose streams are done helps the query with the most tiles left, with a spare
-// candidate buffer, so an estimate that is off costs no idle warps.  The tile is one index
-// block (1024 documents), so the window of every term's postings inside a tile is
-// [block_starts[b][t], block_starts[b+1][t]) with no search.  The warp owns the tile's
-// fp32 accumulators, so every (query, document) cell has exactly one writer, and the
-// result does not depend on which warp scored which tile.
+// Work decomposition.  A work item is one (document tile, query) pair.  Warps take items
+// from one global counter in tile-major order, so the whole GPU works on a window of a few
+// tiles at any moment (their postings and dense head rows stay in L2) and no warp idles
+// while items are left.  The tile is one index block (1024 documents), so the window of
+// every term's postings inside a tile is [block_starts[b][t], block_starts[b+1][t]) with
+// no search.  The warp owns the tile's fp32 accumulators, so every (query, document) cell
+// has exactly one writer, and the result does not depend on which warp scored which item.
+//
+// Candidates.  Each query has one candidate buffer shared by all warps, with a
+// reservation counter (resv), a written counter (done) and a generation.  A warp reserves
+// room for its keys with one atomicAdd; below the capacity it writes them and adds their
+// count to done.  The warp whose reservation crosses the capacity writes its keys into the
+// buffer's spare tail, waits until done reaches its reservation (every earlier writer has
+// finished), keeps the k largest keys, publishes the k-th as the query's threshold and
+// reopens the buffer (done = resv = k, generation + 1).  Warps that reserved past the
+// capacity wait for the generation to change and retry against the raised threshold.
+// Every wait is bounded; one that runs out records a fault, and the merge then reports
+// NaN scores instead of a result.
 //
 // Per tile:
 //  1. head terms (the index's densest terms, stored as dense rows): the warp keeps the
@@ -26,11 +32,8 @@
 //     runs are flattened into full 32-lane chunks, and lanes that hit the same document
 //     (different terms) are applied in term order, one rank at a time (match_any);
 //  3. every score becomes a packed key (order-preserving score bits << 32 | ~doc id:
-//     larger is better, ties go to the lower doc id) and keys at or above the stream's
-//     threshold go to the stream's candidate buffer; on overflow the warp radix-selects
-//     the k-th largest key, compacts the buffer to exactly k keys and raises the
-//     threshold, which it also publishes (atomicMax) as a lower bound for the query's
-//     other streams.  A discarded key is beaten by k kept keys, so the final top-k
+//     larger is better, ties go to the lower doc id) and the keys whose score reaches the
+//     query's threshold go to its candidate buffer.  A discarded key is beaten by k kept keys, so the final top-k
 //     (merge_kernel in select.cu) is exact.
 // Each cell therefore accumulates acc = fma(q_w, d_w, acc) in a fixed order -- head terms
 // by term id, then tail terms by term id, a repeated term in query-slot order -- with one
@@ -60,7 +63,7 @@ constexpr int kPlanThreads = 256;
 constexpr int kMaxWidth = 4096;   // query slots (W) supported
 constexpr int kTile = 1024;       // documents per tile = index block
 constexpr int kLongRun = 48;      // tail windows at least this long are streamed on their own
-constexpr int kMaxHelp = 32;      // spare buffers one query can receive
+constexpr int kSpinLimit = 1 << 21;   // polls of a bounded wait (about a second)
 
 struct ScoreParams {
   const int32_t* doc_ids;
@@ -78,15 +81,8 @@ struct ScoreParams {
   int32_t B;
   int32_t k;
   int32_t ecap;      // plan capacity per query (= W)
-  int32_t C;         // candidate buffer capacity per stream
-  int32_t n_streams; // streams over all queries (>= B)
-  int32_t n_spare;   // spare candidate buffers for helping warps
-  const int32_t* first_stream;   // [B+1]: streams of query q are [first_stream[q], first_stream[q+1])
-  int64_t* work;                 // [B]: estimated work of each query (plan output)
-  int32_t* next_block;           // [B]: next tile of each query (zeroed per call)
-  int32_t* help_count;           // [B]: spare buffers registered to each query (zeroed)
-  int32_t* spare_next;           // [1]: spare buffers handed out (zeroed)
-  int32_t* help_list;            // [B, kMaxHelp]: spare buffer ids of each query
+  int32_t cap;       // candidate buffer capacity per query (keys), > k
+  int64_t cand_stride;   // keys per query buffer: cap + kTile spare slots for the crossing warp
   // plan, per query: head entries and tail runs
   const int32_t* n_head_e;
   const uint16_t* head_h;
@@ -98,9 +94,13 @@ struct ScoreParams {
   const uint16_t* run_end;
   const float* run_w0;
   const float* ent_w;
-  uint64_t* cand;
-  int32_t* cand_cnt;
-  unsigned long long* gthr;   // per query: largest published lower bound of its k-th key
+  uint64_t* cand;              // [B, cand_stride]
+  unsigned long long* gthr;    // [B] published lower bound of each query's k-th key (zeroed)
+  int32_t* resv;               // [B] reserved slots (zeroed)
+  int32_t* done;               // [B] written slots (zeroed); final candidate counts
+  uint32_t* gen;               // [B] buffer generation (zeroed)
+  unsigned long long* item_next;   // next work item (zeroed)
+  int32_t* fault;              // a bounded wait ran out (zeroed)
 };
 
 namespace {
@@ -213,67 +213,6 @@ plan_kernel(const int32_t* __restrict__ qi, const float* __restrict__ qs, int32_
     const_cast<int32_t*>(p.n_head_e)[q] = s_head;
     const_cast<int32_t*>(p.n_runs)[q] = s_runs;
   }
-  // work estimate: ~6 dense-row elements per tail posting, one per head row per document
-  int64_t wk = 0;
-  for (int32_t r = threadIdx.x; r < s_runs; r += blockDim.x) wk += p.lengths[run_term[r]];
-  __shared__ unsigned long long s_wk;
-  if (threadIdx.x == 0) s_wk = 0;
-  __syncthreads();
-  atomicAdd(&s_wk, (unsigned long long)wk);
-  __syncthreads();
-  if (threadIdx.x == 0) p.work[q] = 6 * int64_t(s_wk) + int64_t(s_head + 1) * p.n_docs;
-}
-
-// first_stream[q] = q + floor((S - B) * work_before(q) / total_work): every query gets at
-// least one stream, the rest in proportion to its work.  One CTA.
-__global__ void __launch_bounds__(1024) streams_kernel(const int64_t* __restrict__ work, int32_t B,
-                                                        int32_t S, int32_t* __restrict__ first) {
-  __shared__ long long s_carry, s_tot;
-  __shared__ long long warp_sum[32];
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  // total work
-  long long t = 0;
-  for (int32_t q = threadIdx.x; q < B; q += blockDim.x) t += work[q];
-  for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(FULL, t, o);
-  if (lane == 0) warp_sum[wid] = t;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    long long a = 0;
-    for (int w = 0; w < int(blockDim.x >> 5); ++w) a += warp_sum[w];
-    s_tot = a > 0 ? a : 1;
-    s_carry = 0;
-  }
-  __syncthreads();
-  const long long tot = s_tot;
-  const long long extra = (long long)S - B;
-  for (int32_t q0 = 0; q0 < B; q0 += blockDim.x) {
-    const int32_t q = q0 + threadIdx.x;
-    const long long v = q < B ? work[q] : 0;
-    long long x = v;
-    for (int o = 1; o < 32; o <<= 1) {
-      const long long y = __shfl_up_sync(FULL, x, o);
-      if (lane >= o) x += y;
-    }
-    __syncthreads();
-    if (lane == 31) warp_sum[wid] = x;
-    __syncthreads();
-    long long before = s_carry;
-    for (int w = 0; w < wid; ++w) before += warp_sum[w];
-    before += x - v;
-    if (q < B) {
-      long long f = (long long)((double)extra * (double)before / (double)tot);
-      f = f < 0 ? 0 : (f > extra ? extra : f);   // first[] stays strictly increasing, < S
-      first[q] = int32_t(q + f);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      long long a = 0;
-      for (int w = 0; w < int(blockDim.x >> 5); ++w) a += warp_sum[w];
-      s_carry += a;
-    }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) first[B] = S;
 }
 
 // ---------------------------------------------------------------------------- scoring
@@ -287,6 +226,7 @@ struct WarpLayout {
 
 // Radix-select the k-th largest key of buf[0..n) (n > k, keys distinct), keep exactly the
 // k largest in place (stable) and return the smallest key value that is kept-or-better.
+// The buffer is written by warps of other SMs, so it is read through L2 (ld.global.cg).
 __device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t k,
                                  uint32_t* __restrict__ hist) {
   const int lane = lane_id();
@@ -298,7 +238,7 @@ __device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t 
     const uint64_t pmask = shift == 56 ? 0ull : (~0ull << (shift + 8));
     for (int32_t i0 = 0; i0 < n; i0 += 32) {
       const int32_t i = i0 + lane;
-      const uint64_t key = i < n ? buf[i] : 0ull;
+      const uint64_t key = i < n ? __ldcg(buf + i) : 0ull;
       const bool live = i < n && (key & pmask) == prefix;
       const uint32_t dig = live ? uint32_t((key >> shift) & 255u) : 0x100u;
       const uint32_t peers = __match_any_sync(FULL, dig);
@@ -342,7 +282,7 @@ __device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t 
   int32_t out = 0;
   for (int32_t i0 = 0; i0 < n; i0 += 32) {
     const int32_t i = i0 + lane;
-    const uint64_t key = i < n ? buf[i] : 0ull;
+    const uint64_t key = i < n ? __ldcg(buf + i) : 0ull;
     const bool keep = i < n && key >= prefix;
     const uint32_t bal = __ballot_sync(FULL, keep);
     if (keep) buf[out + __popc(bal & lanemask_lt())] = key;
@@ -469,6 +409,103 @@ __device__ __forceinline__ int32_t lane_scan(int32_t x) {
   return x;
 }
 
+// Bounded polls of a word that other warps of this launch update (read through L2).
+__device__ __forceinline__ bool wait_equal(const int32_t* a, int32_t v) {
+  for (int i = 0; i < kSpinLimit; ++i) {
+    if (*reinterpret_cast<const volatile int32_t*>(a) == v) return true;
+    __nanosleep(64);
+  }
+  return false;
+}
+__device__ __forceinline__ bool wait_change(const uint32_t* a, uint32_t v) {
+  for (int i = 0; i < kSpinLimit; ++i) {
+    if (*reinterpret_cast<const volatile uint32_t*>(a) != v) return true;
+    __nanosleep(64);
+  }
+  return false;
+}
+
+// Per-query state of the shared candidate buffers.
+struct QueryBuf {
+  uint64_t* buf;
+  unsigned long long* gthr;
+  int32_t* resv;
+  int32_t* done;
+  uint32_t* gen;
+  int32_t* fault;
+  int32_t cap, k;
+};
+
+// Appends the tile's documents whose score reaches threshold key thr (marked in m) to a
+// query's shared candidate buffer, following the reservation protocol described at the
+// top of the file.  Called only for tiles with a candidate.
+__device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restrict__ acc, uint32_t span,
+                                               uint32_t dbase, uint32_t* __restrict__ hist, uint64_t thr,
+                                               uint32_t m) {
+  const int lane = lane_id();
+  uint64_t* __restrict__ buf = qb.buf;
+  for (bool first = true;; first = false) {
+    if (!first) m = mark_tile(acc, lane, span, thr);
+    const int32_t cnt = __popc(m);
+    const int32_t incl = lane_scan(cnt);
+    const int32_t total = __shfl_sync(FULL, incl, 31);
+    if (total == 0) return;
+    uint32_t g0 = 0;
+    int32_t pos = 0;
+    if (lane == 0) {
+      g0 = *reinterpret_cast<const volatile uint32_t*>(qb.gen);
+      pos = atomicAdd(qb.resv, total);
+    }
+    g0 = __shfl_sync(FULL, g0, 0);
+    pos = __shfl_sync(FULL, pos, 0);
+    if (pos <= qb.cap) {
+      // below the capacity: write the keys (a crossing reservation runs into the spare tail)
+      int32_t o = pos + incl - cnt;
+      while (m) {
+        const int bit = __ffs(m) - 1;
+        m &= m - 1;
+        const int32_t col = 128 * (bit >> 2) + 4 * lane + (bit & 3);
+        buf[o++] = pack_key(acc[col], dbase + uint32_t(col));
+      }
+      __syncwarp();
+      if (pos + total <= qb.cap) {
+        __threadfence();
+        if (lane == 0) atomicAdd(qb.done, total);
+        return;
+      }
+      // this warp crossed the capacity: once every earlier reservation is written, keep
+      // the k largest keys, publish the k-th as the threshold and reopen the buffer
+      bool ok = true;
+      if (lane == 0) ok = wait_equal(qb.done, pos);
+      ok = __shfl_sync(FULL, int(ok), 0) != 0;
+      if (!ok && lane == 0) atomicOr(qb.fault, 1);
+      __threadfence();
+      const uint64_t t = warp_compact(buf, pos + total, qb.k, hist);
+      __threadfence();
+      if (lane == 0) {
+        atomicMax(qb.gthr, (unsigned long long)t);
+        atomicExch(qb.done, qb.k);
+        __threadfence();
+        atomicExch(qb.resv, qb.k);
+        __threadfence();
+        atomicAdd(qb.gen, 1u);
+      }
+      __syncwarp();
+      return;
+    }
+    // another warp is compacting: wait for the buffer to reopen, then retry against the
+    // raised threshold
+    bool ok = true;
+    if (lane == 0) ok = wait_change(qb.gen, g0);
+    ok = __shfl_sync(FULL, int(ok), 0) != 0;
+    if (!ok) {
+      if (lane == 0) atomicOr(qb.fault, 1);
+      return;
+    }
+    thr = max(thr, uint64_t(__ldcg(qb.gthr)));
+  }
+}
+
 template <typename WT>
 __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 score_kernel(const ScoreParams p) {
@@ -480,55 +517,16 @@ score_kernel(const ScoreParams p) {
   const WT* __restrict__ wts = static_cast<const WT*>(p.weights);
   const WT* __restrict__ hrows = static_cast<const WT*>(p.head_rows);
   const int32_t* __restrict__ doc_ids = p.doc_ids;
-  const int32_t nwarps = int32_t(gridDim.x) * kWarps;
-  int32_t sid = blockIdx.x * kWarps + wid;
+  const unsigned long long n_items = (unsigned long long)p.B * unsigned(p.n_blocks);
+  unsigned long long nit = 0;   // the claimed item (lane 0)
+  if (lane == 0) nit = atomicAdd(p.item_next, 1ull);
   for (;;) {
-    // next assignment: one of this warp's own streams, else a spare buffer for the query
-    // with the most tiles left
-    int32_t q = 0, list = 0;
-    if (sid < p.n_streams) {
-      int32_t lo_q = 0, hi_q = p.B - 1;   // last q with first_stream[q] <= sid
-      while (lo_q < hi_q) {
-        const int32_t mid = (lo_q + hi_q + 1) >> 1;
-        if (p.first_stream[mid] <= sid) lo_q = mid; else hi_q = mid - 1;
-      }
-      q = lo_q;
-      list = sid;
-      sid += nwarps;
-    } else {
-      int32_t best = -1, best_q = 0;
-      for (int32_t qq = lane; qq < p.B; qq += 32) {
-        const int32_t rem = p.n_blocks - __ldcg(p.next_block + qq);
-        if (rem > best) {
-          best = rem;
-          best_q = qq;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        const int32_t ob = __shfl_xor_sync(FULL, best, o), oq = __shfl_xor_sync(FULL, best_q, o);
-        if (ob > best || (ob == best && oq < best_q)) {
-          best = ob;
-          best_q = oq;
-        }
-      }
-      if (best < 2) break;   // a tile or less left anywhere: the owners finish it
-      int32_t hb = 0, slot = 0;
-      if (lane == 0) {
-        hb = atomicAdd(p.spare_next, 1);
-        if (hb < p.n_spare) slot = atomicAdd(p.help_count + best_q, 1);
-      }
-      hb = __shfl_sync(FULL, hb, 0);
-      slot = __shfl_sync(FULL, slot, 0);
-      if (hb >= p.n_spare) break;
-      list = p.n_streams + hb;
-      if (slot >= kMaxHelp) {
-        if (lane == 0) p.cand_cnt[list] = 0;
-        break;
-      }
-      if (lane == 0) p.help_list[int64_t(best_q) * kMaxHelp + slot] = hb;
-      q = best_q;
-    }
+    const unsigned long long it = __shfl_sync(FULL, nit, 0);
+    if (it >= n_items) break;
+    // claim the next item now, so the atomic's round trip overlaps this item's work
+    if (lane == 0) nit = atomicAdd(p.item_next, 1ull);
+    const int32_t b = int32_t(it / unsigned(p.B));
+    const int32_t q = int32_t(it - (unsigned long long)b * unsigned(p.B));
     const int64_t pbase = int64_t(q) * p.ecap;
     const int32_t nhe = p.n_head_e[q];
     const int32_t nr = p.n_runs[q];
@@ -540,17 +538,7 @@ score_kernel(const ScoreParams p) {
     const uint16_t* __restrict__ run_end = p.run_end + pbase;
     const float* __restrict__ run_w0 = p.run_w0 + pbase;
     const float* __restrict__ ent_w = p.ent_w + pbase;
-    uint64_t* __restrict__ buf = p.cand + int64_t(list) * p.C;
-    uint64_t thr = __ldcg(p.gthr + q);
-    int32_t nbuf = 0;
-
-    int32_t nb = 0;   // the claimed tile (lane 0)
-    if (lane == 0) nb = atomicAdd(p.next_block + q, 1);
-    for (;;) {
-      const int32_t b = __shfl_sync(FULL, nb, 0);
-      if (b >= p.n_blocks) break;
-      // claim the next tile now, so the atomic's round trip overlaps this tile's work
-      if (lane == 0) nb = atomicAdd(p.next_block + q, 1);
+    {
       const int32_t d0i = b * kTile;
       const int32_t d1 = int32_t(min64(int64_t(b + 1) * kTile, p.n_docs));
       const uint32_t span = uint32_t(d1 - d0i);
@@ -676,62 +664,35 @@ score_kernel(const ScoreParams p) {
       }
       __syncwarp();
 
-      // 3. fused selection.  Every lane reads its 32 accumulators (documents 128 * i +
-      // 4 * lane + j) with vector loads and marks those whose score reaches the threshold's
-      // score; the marked documents' keys are appended to the buffer at per-lane offsets
-      // (a superset of the keys >= thr is harmless: only the k largest survive).  The
-      // buffer holds at least k + kTile keys, so after a compaction a tile always fits.
-      thr = max(thr, uint64_t(g_pub));
-      uint32_t m = mark_tile(acc, lane, span, thr);
-      int32_t cnt = __popc(m);
-      if (__any_sync(FULL, cnt != 0)) {
-        int32_t incl = lane_scan(cnt);
-        int32_t total = __shfl_sync(FULL, incl, 31);
-        if (nbuf + total > p.C) {
-          thr = warp_compact(buf, nbuf, p.k, hist);
-          nbuf = p.k;
-          if (lane == 0) atomicMax(p.gthr + q, (unsigned long long)thr);
-          m = mark_tile(acc, lane, span, thr);
-          cnt = __popc(m);
-          incl = lane_scan(cnt);
-          total = __shfl_sync(FULL, incl, 31);
-        }
-        int32_t o = nbuf + incl - cnt;
-        const uint32_t dbase = uint32_t(p.doc_base + d0i);
-        while (m) {
-          const int bit = __ffs(m) - 1;
-          m &= m - 1;
-          const int32_t col = 128 * (bit >> 2) + 4 * lane + (bit & 3);
-          buf[o++] = pack_key(acc[col], dbase + uint32_t(col));
-        }
-        nbuf += total;
-        __syncwarp();
+      // 3. fused selection: the documents whose score reaches the query's threshold go to
+      // its candidate buffer (a superset of the keys >= threshold is harmless: only the k
+      // largest survive the compactions and the merge)
+      const uint64_t thr = uint64_t(g_pub);
+      const uint32_t m = mark_tile(acc, lane, span, thr);
+      if (__any_sync(FULL, m != 0u)) {
+        QueryBuf qb{p.cand + int64_t(q) * p.cand_stride, p.gthr + q, p.resv + q, p.done + q, p.gen + q,
+                    p.fault, p.cap, p.k};
+        append_candidates(qb, acc, span, uint32_t(p.doc_base + d0i), hist, thr, m);
       }
     }
-    if (nbuf > p.k) {
-      const uint64_t t2 = warp_compact(buf, nbuf, p.k, hist);
-      nbuf = p.k;
-      if (lane == 0) atomicMax(p.gthr + q, (unsigned long long)t2);
-    }
-    if (lane == 0) p.cand_cnt[list] = nbuf;
-    __syncwarp();
   }
 }
 
 struct Cfg {
-  int npow2 = 0, S = 0, H = 0, C = 0, smem = 0, ctas_per_sm = 0, grid = 0;
-  int64_t ecap = 0, n_blocks = 0, kk = 0;
+  int npow2 = 0, cap = 0, smem = 0, ctas_per_sm = 0, grid = 0;
+  int64_t ecap = 0, n_blocks = 0, kk = 0, stride = 0;
   int64_t off_nhe = 0, off_hh = 0, off_hw = 0, off_hs = 0, off_nruns = 0, off_rterm = 0, off_rb32 = 0,
-          off_rend = 0, off_rw0 = 0, off_entw = 0, off_cand = 0, off_cnt = 0, off_first = 0,
-          off_work = 0, off_hlist = 0, off_zero = 0, zero_bytes = 0, total = 0;
+          off_rend = 0, off_rw0 = 0, off_entw = 0, off_cand = 0, off_zero = 0, zero_bytes = 0, total = 0;
 };
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+int64_t align8(int64_t x) { return (x + 7) / 8 * 8; }
 
-// Workspace layout of one call for the configured stream count.
+// Workspace layout of one call for the configured buffer capacity.
 void set_layout(Cfg& c, int64_t B) {
   int64_t o = 0;
   const int64_t E = B * c.ecap;
+  c.stride = c.cap + kTile;
   c.off_nhe = o; o = align256(o + B * 4);
   c.off_hh = o; o = align256(o + E * 2);
   c.off_hw = o; o = align256(o + E * 4);
@@ -742,13 +703,10 @@ void set_layout(Cfg& c, int64_t B) {
   c.off_rend = o; o = align256(o + E * 2);
   c.off_rw0 = o; o = align256(o + E * 4);
   c.off_entw = o; o = align256(o + E * 4);
-  c.off_cand = o; o = align256(o + int64_t(c.S + c.H) * c.C * 8);
-  c.off_cnt = o; o = align256(o + int64_t(c.S + c.H) * 4);
-  c.off_first = o; o = align256(o + (B + 1) * 4);
-  c.off_work = o; o = align256(o + B * 8);
-  c.off_hlist = o; o = align256(o + B * kMaxHelp * 4);
-  // cleared by every call: thresholds [B] u64, next tile [B], help counts [B], spare counter
-  c.off_zero = o; c.zero_bytes = B * 8 + B * 4 + B * 4 + 4; o = align256(o + c.zero_bytes);
+  c.off_cand = o; o = align256(o + B * c.stride * 8);
+  // cleared by every call: thresholds [B] u64, resv [B], done [B], generation [B],
+  // item counter u64, fault flag
+  c.off_zero = o; c.zero_bytes = align8(B * 8 + 3 * B * 4) + 16; o = align256(o + c.zero_bytes);
   c.total = o;
 }
 
@@ -774,14 +732,11 @@ int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) 
   c.npow2 = kPlanThreads;
   while (c.npow2 < W) c.npow2 <<= 1;
   c.n_blocks = (ix->n_docs + kTile - 1) / kTile;
-  // one stream per resident warp (at least one per query)
-  const int64_t warps = int64_t(sms) * c.ctas_per_sm * kWarps;
-  c.S = int(std::max<int64_t>(warps, B));
-  c.H = c.S;
-  c.grid = int(std::min<int64_t>(int64_t(sms) * c.ctas_per_sm, (c.S + kWarps - 1) / kWarps));
-  // room for k kept keys plus one whole tile, so a tile's candidates always fit after a
-  // compaction
-  c.C = int(((std::max<int64_t>(2 * c.kk, c.kk + kTile) + 31) / 32) * 32);
+  // one persistent CTA per resident slot; fewer when the batch has fewer items
+  const int64_t items = B * c.n_blocks;
+  c.grid = int(std::max<int64_t>(1, std::min<int64_t>(int64_t(sms) * c.ctas_per_sm, (items + kWarps - 1) / kWarps)));
+  // a compaction keeps k keys; the rest of the capacity takes several tiles' candidates
+  c.cap = int(((std::max<int64_t>(4 * c.kk, c.kk + 4 * kTile) + 31) / 32) * 32);
   set_layout(c, B);
   return GSP_OK;
 }
@@ -867,9 +822,8 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.B = int32_t(B);
   p.k = int32_t(c.kk);
   p.ecap = int32_t(c.ecap);
-  p.C = c.C;
-  p.n_streams = c.S;
-  p.n_spare = c.H;
+  p.cap = c.cap;
+  p.cand_stride = c.stride;
   p.n_head_e = reinterpret_cast<int32_t*>(w + c.off_nhe);
   p.head_h = reinterpret_cast<uint16_t*>(w + c.off_hh);
   p.head_w = reinterpret_cast<float*>(w + c.off_hw);
@@ -881,23 +835,20 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.run_w0 = reinterpret_cast<float*>(w + c.off_rw0);
   p.ent_w = reinterpret_cast<float*>(w + c.off_entw);
   p.cand = reinterpret_cast<uint64_t*>(w + c.off_cand);
-  p.cand_cnt = reinterpret_cast<int32_t*>(w + c.off_cnt);
-  p.first_stream = reinterpret_cast<int32_t*>(w + c.off_first);
-  p.work = reinterpret_cast<int64_t*>(w + c.off_work);
-  p.help_list = reinterpret_cast<int32_t*>(w + c.off_hlist);
-  p.gthr = reinterpret_cast<unsigned long long*>(w + c.off_zero);
-  p.next_block = reinterpret_cast<int32_t*>(w + c.off_zero + B * 8);
-  p.help_count = p.next_block + B;
-  p.spare_next = p.help_count + B;
-  GSP_CUDA(cudaMemsetAsync(w + c.off_zero, 0, size_t(c.zero_bytes), st));
+  char* z = w + c.off_zero;
+  p.gthr = reinterpret_cast<unsigned long long*>(z);
+  p.resv = reinterpret_cast<int32_t*>(z + B * 8);
+  p.done = p.resv + B;
+  p.gen = reinterpret_cast<uint32_t*>(p.done + B);
+  p.item_next = reinterpret_cast<unsigned long long*>(z + align8(B * 8 + 3 * B * 4));
+  p.fault = reinterpret_cast<int32_t*>(p.item_next + 1);
+  GSP_CUDA(cudaMemsetAsync(z, 0, size_t(c.zero_bytes), st));
 
   const size_t plan_smem = size_t(c.npow2) * 8;
   GSP_CUDA(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(plan_smem)));
   plan_kernel<<<unsigned(B), kPlanThreads, plan_smem, st>>>(
       qi, qs, int32_t(B), int32_t(W), ix->V, c.npow2, ix->offsets, ix->head_slot, ix->n_head,
       ix->wdtype == GSP_W_U8 ? ix->term_scale : nullptr, p);
-  GSP_CHECK_LAUNCH();
-  streams_kernel<<<1, 1024, 0, st>>>(p.work, int32_t(B), c.S, const_cast<int32_t*>(p.first_stream));
   GSP_CHECK_LAUNCH();
 
   if (c.n_blocks > 0) {
@@ -909,8 +860,8 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
     }
     if (rc) return rc;
   }
-  return merge_streams_device(p.cand, B, p.first_stream, p.help_list, p.help_count, kMaxHelp, c.S, c.C,
-                              p.cand_cnt, c.kk, out_scores, out_ids, out_keys, st);
+  return merge_topk_device(p.cand, B, 1, c.stride, 0, p.done, 1, nullptr, c.kk, out_scores, out_ids,
+                           out_keys, st, -1, p.fault);
 }
 
 extern "C" int gsp_profile_enable(int on) {
@@ -996,24 +947,22 @@ extern "C" int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* q
   if (rc) return rc;
   // fewer streams shrink the candidate buffers; the result does not depend on the stream
   // count, only the parallelism does
-  while (c.total > int64_t(kNoAllocScratchBytes) && (c.S > B || c.H > 0)) {
-    if (c.H > 0) {
-      c.H /= 2;
-    } else {
-      c.S = int(std::max<int64_t>(B, c.S / 2));
-    }
+  // a smaller candidate capacity means more frequent compactions, never another result;
+  // the smallest one keeps k keys plus a whole tile
+  const int min_cap = int(((c.kk + kTile + 31) / 32) * 32);
+  while (c.total > int64_t(kNoAllocScratchBytes) && c.cap > min_cap) {
+    c.cap = std::max(min_cap, c.cap / 2 / 32 * 32);
     set_layout(c, B);
   }
   GSP_REQUIRE(c.total <= int64_t(kNoAllocScratchBytes), GSP_ERR_UNSUPPORTED,
               "gsp_score_topk_noalloc: this batch needs %lld bytes of scratch, more than the "
               "fixed %lld (lower the batch size or top_k, or use gsp_score_topk with a workspace)",
               (long long)c.total, (long long)kNoAllocScratchBytes);
-  c.grid = int(std::min<int64_t>(int64_t(num_sms()) * c.ctas_per_sm, (c.S + kWarps - 1) / kWarps));
   void* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
   // Every buffer in the scratch is written before it is read within a call except the
-  // per-query thresholds and tile counters and the spare-buffer counters, which
+  // per-query thresholds and buffer counters, the item counter and the fault flag, which
   // score_with_cfg clears on the stream; the array keeps the previous call's contents
   // otherwise.
   return score_with_cfg(ix, qi, qs, B, W, c, out_scores, out_ids, out_keys, scratch, as_stream(stream));

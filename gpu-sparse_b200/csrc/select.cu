@@ -28,40 +28,24 @@ struct CountsParam {
 
 namespace {
 
-// The ragged list set of the scorer: query b owns the lists [first[b], first[b+1]) and the
-// spare lists S + help_list[b * max_help + m], m < min(help_count[b], max_help).
-struct Ragged {
-  const int32_t* first;
-  const int32_t* help_list;
-  const int32_t* help_count;
-  int32_t max_help, S;
-};
-
-// The candidate lists of one query, numbered r in [0, n): either R lists at kb + r *
-// stride_r with counts from the kernel parameter or from counts_dev[b * cstride_b + r], or
-// (ragged) the query's lists of a Ragged set at keys + id * stride_r, counts_dev[id].
+// The R candidate lists of one query at kb + r * stride_r, with counts from the kernel
+// parameter or from counts_dev[b * cstride_b + r].
 struct Lists {
   const uint64_t* base;
   int64_t stride_r;
   const int32_t* counts_dev;
   int64_t cstride_b;
-  const int32_t* help;   // ragged: this query's spare list ids
-  int32_t b, n, own, first, S;
-  bool ragged, use_param;
-  __device__ __forceinline__ int32_t id(int32_t r) const {
-    if (!ragged) return r;
-    return r < own ? first + r : S + help[r - own];
-  }
+  int32_t b, n;
+  bool use_param;
   __device__ __forceinline__ int32_t count(int32_t r, const CountsParam& cp) const {
-    if (ragged) return counts_dev[id(r)];
     return use_param ? cp.c[r] : counts_dev[int64_t(b) * cstride_b + r];
   }
-  __device__ __forceinline__ const uint64_t* list(int32_t r) const { return base + int64_t(id(r)) * stride_r; }
+  __device__ __forceinline__ const uint64_t* list(int32_t r) const { return base + int64_t(r) * stride_r; }
 };
 
 __global__ void __launch_bounds__(kMergeThreads)
 merge_kernel(const uint64_t* __restrict__ keys, int64_t stride_b, int64_t stride_r, int32_t R,
-             const Ragged rg, const int32_t* __restrict__ counts_dev, int64_t cstride_b,
+             const int32_t* __restrict__ fault, const int32_t* __restrict__ counts_dev, int64_t cstride_b,
              const CountsParam cp, int32_t use_param, int32_t k, int32_t k_out, int32_t kpow2,
              int64_t pad_id, float* __restrict__ out_s, int64_t* __restrict__ out_i,
              uint64_t* __restrict__ out_k) {
@@ -71,26 +55,24 @@ merge_kernel(const uint64_t* __restrict__ keys, int64_t stride_b, int64_t stride
   __shared__ int32_t s_part[kMergeThreads / 32];
   const int32_t b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int64_t ob = int64_t(b) * k_out;
+  if (fault && *fault) {
+    // the producer of the candidates reported a fault: no result
+    for (int32_t j = tid; j < k_out; j += blockDim.x) {
+      out_s[ob + j] = __int_as_float(0x7fc00000);
+      out_i[ob + j] = -1;
+      if (out_k) out_k[ob + j] = 0ull;
+    }
+    return;
+  }
   Lists L;
-  L.ragged = rg.first != nullptr;
   L.use_param = use_param != 0;
   L.counts_dev = counts_dev;
   L.cstride_b = cstride_b;
   L.stride_r = stride_r;
   L.b = b;
-  L.help = nullptr;
-  L.own = L.first = L.S = 0;
-  if (L.ragged) {
-    L.base = keys;
-    L.first = rg.first[b];
-    L.own = rg.first[b + 1] - L.first;
-    L.S = rg.S;
-    L.help = rg.help_list + int64_t(b) * rg.max_help;
-    L.n = L.own + min(rg.help_count[b], rg.max_help);
-  } else {
-    L.base = keys + int64_t(b) * stride_b;
-    L.n = R;
-  }
+  L.base = keys + int64_t(b) * stride_b;
+  L.n = R;
 
   int32_t part = 0;
   for (int32_t r = tid; r < L.n; r += blockDim.x) part += L.count(r, cp);
@@ -202,7 +184,6 @@ merge_kernel(const uint64_t* __restrict__ keys, int64_t stride_b, int64_t stride
       __syncthreads();
     }
   }
-  const int64_t ob = int64_t(b) * k_out;
   for (int32_t j = tid; j < k_out; j += blockDim.x) {
     if (j < kk && j < n) {
       const uint64_t key = sk[j];
@@ -241,10 +222,10 @@ __global__ void compact_rows_kernel(const float* __restrict__ scores, int64_t L,
 
 }  // namespace
 
-static int launch_merge(const uint64_t* keys, int64_t B, int64_t R, int64_t stride_b, int64_t stride_r,
-                        const Ragged& rg, const int32_t* counts_dev, int64_t cstride_b,
-                        const int32_t* counts_host, int64_t k, float* out_scores, int64_t* out_ids,
-                        uint64_t* out_keys, cudaStream_t st, int64_t pad_id) {
+int merge_topk_device(const uint64_t* keys, int64_t B, int64_t R, int64_t stride_b, int64_t stride_r,
+                      const int32_t* counts_dev, int64_t cstride_b, const int32_t* counts_host,
+                      int64_t k, float* out_scores, int64_t* out_ids, uint64_t* out_keys,
+                      cudaStream_t st, int64_t pad_id, const int32_t* fault) {
   GSP_REQUIRE(B >= 0 && R >= 1 && k >= 0, GSP_ERR_ARG, "merge: bad arguments");
   GSP_REQUIRE(k <= kMaxK, GSP_ERR_UNSUPPORTED, "merge: k %lld exceeds the supported maximum %d",
               (long long)k, kMaxK);
@@ -262,30 +243,12 @@ static int launch_merge(const uint64_t* keys, int64_t B, int64_t R, int64_t stri
   while (kpow2 < k) kpow2 <<= 1;
   const size_t smem = size_t(kpow2) * 8;
   GSP_CUDA(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  merge_kernel<<<unsigned(B), kMergeThreads, smem, st>>>(keys, stride_b, stride_r, int32_t(R), rg,
+  merge_kernel<<<unsigned(B), kMergeThreads, smem, st>>>(keys, stride_b, stride_r, int32_t(R), fault,
                                                          counts_dev, cstride_b, cp, use_param, int32_t(k),
                                                          int32_t(k), kpow2, pad_id, out_scores, out_ids,
                                                          out_keys);
   GSP_CHECK_LAUNCH();
   return GSP_OK;
-}
-
-int merge_topk_device(const uint64_t* keys, int64_t B, int64_t R, int64_t stride_b, int64_t stride_r,
-                      const int32_t* counts_dev, int64_t cstride_b, const int32_t* counts_host,
-                      int64_t k, float* out_scores, int64_t* out_ids, uint64_t* out_keys,
-                      cudaStream_t st, int64_t pad_id) {
-  const Ragged none{nullptr, nullptr, nullptr, 0, 0};
-  return launch_merge(keys, B, R, stride_b, stride_r, none, counts_dev, cstride_b, counts_host, k,
-                      out_scores, out_ids, out_keys, st, pad_id);
-}
-
-int merge_streams_device(const uint64_t* keys, int64_t B, const int32_t* first, const int32_t* help_list,
-                         const int32_t* help_count, int32_t max_help, int32_t S, int64_t stride,
-                         const int32_t* counts_dev, int64_t k, float* out_scores, int64_t* out_ids,
-                         uint64_t* out_keys, cudaStream_t st) {
-  const Ragged rg{first, help_list, help_count, max_help, S};
-  return launch_merge(keys, B, 1, 0, stride, rg, counts_dev, 0, nullptr, k, out_scores, out_ids,
-                      out_keys, st, -1);
 }
 
 }  // namespace gsp
