@@ -33,8 +33,8 @@
 //     (different terms) are applied in term order, one rank at a time (match_any);
 //  3. every score becomes a packed key (order-preserving score bits << 32 | ~doc id:
 //     larger is better, ties go to the lower doc id) and the keys whose score reaches the
-//     query's threshold go to its candidate buffer.  A discarded key is beaten by k kept keys, so the final top-k
-//     (merge_kernel in select.cu) is exact.
+//     query's threshold go to its candidate buffer.  A discarded key is beaten by k kept
+//     keys, so the final top-k (merge_kernel in select.cu) is exact.
 // Each cell therefore accumulates acc = fma(q_w, d_w, acc) in a fixed order -- head terms
 // by term id, then tail terms by term id, a repeated term in query-slot order -- with one
 // fp32 rounding per fused multiply-add: bitwise reproducible, and equal to the CPU
@@ -64,6 +64,7 @@ constexpr int kMaxWidth = 4096;   // query slots (W) supported
 constexpr int kTile = 1024;       // documents per tile = index block
 constexpr int kLongRun = 48;      // tail windows at least this long are streamed on their own
 constexpr int kSpinLimit = 1 << 21;   // polls of a bounded wait (about a second)
+constexpr int kCompactUnroll = 8;     // keys per lane loaded together by a compaction pass
 
 struct ScoreParams {
   const int32_t* doc_ids;
@@ -230,20 +231,54 @@ struct WarpLayout {
 __device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t k,
                                  uint32_t* __restrict__ hist) {
   const int lane = lane_id();
-  uint64_t prefix = 0;
+  // All keys share the bytes above the highest bit where the smallest and largest differ;
+  // the digit passes start below them.  Every pass issues kCompactUnroll loads per lane
+  // before it uses any.
+  uint64_t mn = ~0ull, mx = 0ull;
+  for (int32_t i0 = 0; i0 < n; i0 += 32 * kCompactUnroll) {
+    uint64_t kk[kCompactUnroll];
+#pragma unroll
+    for (int u = 0; u < kCompactUnroll; ++u) {
+      const int32_t i = i0 + 32 * u + lane;
+      kk[u] = i < n ? __ldcg(buf + i) : 0ull;
+    }
+#pragma unroll
+    for (int u = 0; u < kCompactUnroll; ++u) {
+      if (i0 + 32 * u + lane < n) {
+        mn = min(mn, kk[u]);
+        mx = max(mx, kk[u]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    mn = min(mn, (uint64_t)__shfl_xor_sync(FULL, (unsigned long long)mn, o));
+    mx = max(mx, (uint64_t)__shfl_xor_sync(FULL, (unsigned long long)mx, o));
+  }
+  const uint64_t diff = mn ^ mx;
+  const int top = diff ? 63 - __clzll((long long)diff) : 0;
+  const int start = (top / 8) * 8;
+  uint64_t prefix = start == 56 ? 0ull : (mn & (~0ull << (start + 8)));
   int32_t need = k;
-  for (int shift = 56; shift >= 0; shift -= 8) {
+  for (int shift = start; shift >= 0; shift -= 8) {
     for (int j = lane; j < 256; j += 32) hist[j] = 0u;
     __syncwarp();
     const uint64_t pmask = shift == 56 ? 0ull : (~0ull << (shift + 8));
-    for (int32_t i0 = 0; i0 < n; i0 += 32) {
-      const int32_t i = i0 + lane;
-      const uint64_t key = i < n ? __ldcg(buf + i) : 0ull;
-      const bool live = i < n && (key & pmask) == prefix;
-      const uint32_t dig = live ? uint32_t((key >> shift) & 255u) : 0x100u;
-      const uint32_t peers = __match_any_sync(FULL, dig);
-      if (live && (peers & lanemask_lt()) == 0u) hist[dig] += __popc(peers);
-      __syncwarp();
+    for (int32_t i0 = 0; i0 < n; i0 += 32 * kCompactUnroll) {
+      uint64_t kk[kCompactUnroll];
+#pragma unroll
+      for (int u = 0; u < kCompactUnroll; ++u) {
+        const int32_t i = i0 + 32 * u + lane;
+        kk[u] = i < n ? __ldcg(buf + i) : 0ull;
+      }
+#pragma unroll
+      for (int u = 0; u < kCompactUnroll; ++u) {
+        const bool live = i0 + 32 * u + lane < n && (kk[u] & pmask) == prefix;
+        const uint32_t dig = live ? uint32_t((kk[u] >> shift) & 255u) : 0x100u;
+        const uint32_t peers = __match_any_sync(FULL, dig);
+        if (live && (peers & lanemask_lt()) == 0u) hist[dig] += __popc(peers);
+        __syncwarp();
+      }
     }
     // digit D with (count above D) < need <= (count above D) + hist[D]
     int32_t s = 0;
@@ -278,15 +313,23 @@ __device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t 
     __syncwarp();
     if (cD == need) break;
   }
-  // stable in-place compaction of keys >= prefix
+  // stable in-place compaction of keys >= prefix (writes never pass the loaded chunks)
   int32_t out = 0;
-  for (int32_t i0 = 0; i0 < n; i0 += 32) {
-    const int32_t i = i0 + lane;
-    const uint64_t key = i < n ? __ldcg(buf + i) : 0ull;
-    const bool keep = i < n && key >= prefix;
-    const uint32_t bal = __ballot_sync(FULL, keep);
-    if (keep) buf[out + __popc(bal & lanemask_lt())] = key;
-    out += __popc(bal);
+  for (int32_t i0 = 0; i0 < n; i0 += 32 * kCompactUnroll) {
+    uint64_t kk[kCompactUnroll];
+#pragma unroll
+    for (int u = 0; u < kCompactUnroll; ++u) {
+      const int32_t i = i0 + 32 * u + lane;
+      kk[u] = i < n ? __ldcg(buf + i) : 0ull;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < kCompactUnroll; ++u) {
+      const bool keep = i0 + 32 * u + lane < n && kk[u] >= prefix;
+      const uint32_t bal = __ballot_sync(FULL, keep);
+      if (keep) buf[out + __popc(bal & lanemask_lt())] = kk[u];
+      out += __popc(bal);
+    }
   }
   __syncwarp();
   return prefix;

@@ -30,7 +30,7 @@ from . import _lib as L
 
 BLOCK_SIZE = 32          # posting lists are padded to a warp (src/gpu_inverted_index.py:18)
 BLOCK_DOCS = 1024        # documents per block_starts row = the scorer's document tile
-N_HEAD = 64              # densest terms scored from dense rows instead of posting lists
+N_HEAD = 128             # densest terms scored from dense rows instead of posting lists
 VOCAB_SIZE = 30522       # src/run_correctness_verification.py:28
 
 
