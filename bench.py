@@ -317,15 +317,12 @@ def run_ours(args):
     peak, peak_src = peaks()
     achieved = balg / (kern_ms * 1e-3) / 1e9
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "score_kernel_traffic.json")
+    tp = os.path.join(ROOT, "profiles", f"score_kernel_traffic_config{args.config}.md")
     if os.path.exists(tp):
-        try:
-            tj = json.load(open(tp))
-            ent = tj.get(f"config{args.config}_gpus{world}")
-            if ent:
-                traffic = ent["dram_bytes_per_launch"]
-        except Exception:
-            traffic = None
+        import re
+        m = re.search(rf"config{args.config}_gpus{world} dram_bytes_per_launch: (\d+)", open(tp).read())
+        if m:
+            traffic = int(m.group(1))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -336,7 +333,7 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
-    launches_per_step = 4 if world == 1 else 5   # plan, streams, score, shard merge (+ global merge)
+    launches_per_step = 3 if world == 1 else 4   # plan, score, shard merge (+ global merge)
     line = {
         "metric": METRIC,
         "value": B * K / (total_ms * 1e-3),

@@ -549,7 +549,8 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
   }
 }
 
-template <typename WT>
+// WT: posting weight type; HT: head row type (WT, or float rows for uint8 postings).
+template <typename WT, typename HT>
 __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 score_kernel(const ScoreParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -558,7 +559,7 @@ score_kernel(const ScoreParams p) {
   float* acc = reinterpret_cast<float*>(wsm + WarpLayout::acc);
   uint32_t* hist = reinterpret_cast<uint32_t*>(wsm + WarpLayout::hist);
   const WT* __restrict__ wts = static_cast<const WT*>(p.weights);
-  const WT* __restrict__ hrows = static_cast<const WT*>(p.head_rows);
+  const HT* __restrict__ hrows = static_cast<const HT*>(p.head_rows);
   const int32_t* __restrict__ doc_ids = p.doc_ids;
   const unsigned long long n_items = (unsigned long long)p.B * unsigned(p.n_blocks);
   unsigned long long nit = 0;   // the claimed item (lane 0)
@@ -598,11 +599,11 @@ score_kernel(const ScoreParams p) {
           const int32_t h = head_h[e];
           const float qw = head_w[e];
           float sc = 1.0f;
-          if constexpr (std::is_same<WT, uint8_t>::value) sc = head_sc[e];
-          const WT* row = hrows + int64_t(h) * p.head_ld + d0i + pofs + 4 * lane;
+          if constexpr (std::is_same<HT, uint8_t>::value) sc = head_sc[e];
+          const HT* row = hrows + int64_t(h) * p.head_ld + d0i + pofs + 4 * lane;
           float4 v[kHeadVec];
 #pragma unroll
-          for (int i = 0; i < kHeadVec; ++i) v[i] = Vec4<WT>::get(row + 128 * i, sc);
+          for (int i = 0; i < kHeadVec; ++i) v[i] = Vec4<HT>::get(row + 128 * i, sc);
 #pragma unroll
           for (int i = 0; i < kHeadVec; ++i) fma4(a[i], qw, v[i]);
         }
@@ -797,9 +798,9 @@ Profile& profile() {
   return p;
 }
 
-template <typename WT>
+template <typename WT, typename HT>
 int launch_score(const ScoreParams& p, const Cfg& c, cudaStream_t st) {
-  auto kern = score_kernel<WT>;
+  auto kern = score_kernel<WT, HT>;
   GSP_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem));
   Profile& pr = profile();
   std::pair<cudaEvent_t, cudaEvent_t>* evp = nullptr;
@@ -895,10 +896,17 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   GSP_CHECK_LAUNCH();
 
   if (c.n_blocks > 0) {
+    // head rows share the postings' type, except that uint8 postings may have fp32 rows
+    const int32_t hdt = ix->n_head > 0 ? ix->head_wdtype : ix->wdtype;
+    GSP_REQUIRE(hdt == ix->wdtype || (ix->wdtype == GSP_W_U8 && hdt == GSP_W_F32), GSP_ERR_ARG,
+                "gsp_score_topk: head rows of type %d do not go with weights of type %d", hdt,
+                ix->wdtype);
     switch (ix->wdtype) {
-      case GSP_W_F32: rc = launch_score<float>(p, c, st); break;
-      case GSP_W_BF16: rc = launch_score<__nv_bfloat16>(p, c, st); break;
-      case GSP_W_U8: rc = launch_score<uint8_t>(p, c, st); break;
+      case GSP_W_F32: rc = launch_score<float, float>(p, c, st); break;
+      case GSP_W_BF16: rc = launch_score<__nv_bfloat16, __nv_bfloat16>(p, c, st); break;
+      case GSP_W_U8:
+        rc = hdt == GSP_W_F32 ? launch_score<uint8_t, float>(p, c, st) : launch_score<uint8_t, uint8_t>(p, c, st);
+        break;
       default: set_error("gsp_score_topk: unknown weight dtype %d", ix->wdtype); return GSP_ERR_ARG;
     }
     if (rc) return rc;

@@ -44,7 +44,7 @@ class IndexView(ctypes.Structure):
         ("doc_ids", ctypes.c_void_p), ("weights", ctypes.c_void_p),
         ("term_scale", ctypes.c_void_p), ("offsets", ctypes.c_void_p),
         ("lengths", ctypes.c_void_p), ("block_starts", ctypes.c_void_p),
-        ("n_head", ctypes.c_int32), ("pad2_", ctypes.c_int32), ("head_slot", ctypes.c_void_p),
+        ("n_head", ctypes.c_int32), ("head_wdtype", ctypes.c_int32), ("head_slot", ctypes.c_void_p),
         ("head_rows", ctypes.c_void_p), ("head_ld", ctypes.c_int64),
     ]
 

@@ -56,6 +56,7 @@ class GPUInvertedIndex:
     head_slot: Optional[torch.Tensor] = None
     head_rows: Optional[torch.Tensor] = None
     head_ld: int = 0
+    head_wdtype: int = 0          # dtype code of head_rows (fp32 rows for uint8 postings)
     _view: object = field(default=None, repr=False, compare=False)
 
 
@@ -190,10 +191,15 @@ def ensure_head(index: GPUInvertedIndex, n_head: int = N_HEAD, head_ids=None) ->
     lengths = index.lengths
     H = min(H, int((lengths > 0).sum().item()))
     wd = getattr(index, "weight_dtype", "fp32")
-    w, code, dt = {"fp32": (index.scores, L.W_F32, torch.float32),
-                   "bf16": (getattr(index, "weights_q", None), L.W_BF16, torch.bfloat16),
-                   "u8": (getattr(index, "weights_q", None), L.W_U8, torch.uint8)}[wd]
     with torch.cuda.device(dev):
+        if wd == "fp32":
+            w, code, dt = index.scores, L.W_F32, torch.float32
+        elif wd == "bf16":
+            w, code, dt = index.weights_q, L.W_BF16, torch.bfloat16
+        else:
+            # uint8 postings: the head rows hold the dequantised weights q * scale_t (the
+            # exact values the scorer computes), so the dense phase needs no decode
+            w, code, dt = dequantized_weights(index), L.W_F32, torch.float32
         if head_ids is not None:
             ids = torch.as_tensor(head_ids, dtype=torch.int64).to(dev).unique().to(torch.int32)
             H = int(ids.numel())
@@ -210,6 +216,7 @@ def ensure_head(index: GPUInvertedIndex, n_head: int = N_HEAD, head_ids=None) ->
                                             L.ptr(index.doc_ids), L.ptr(w), code, ld, L.ptr(rows),
                                             L.stream_of(dev)), "head rows")
     index.head_ids, index.head_slot, index.head_rows, index.head_ld = ids, slot, rows, ld
+    index.head_wdtype = code
 
 
 def view(index: GPUInvertedIndex) -> L.IndexView:
@@ -239,6 +246,7 @@ def view(index: GPUInvertedIndex) -> L.IndexView:
     v.head_slot = index.head_slot.data_ptr()
     v.head_rows = index.head_rows.data_ptr()
     v.head_ld = int(index.head_ld)
+    v.head_wdtype = int(getattr(index, "head_wdtype", code))
     return v
 
 

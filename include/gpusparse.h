@@ -133,9 +133,10 @@ typedef struct gsp_index_view {
     const uint32_t* block_starts;
     /* head terms scored from dense rows instead of their posting lists (n_head may be 0) */
     int32_t n_head;
-    int32_t pad2_;
+    int32_t head_wdtype;       /* GSP_W_* of head_rows: wdtype, or GSP_W_F32 with wdtype
+                                  GSP_W_U8 (rows hold the dequantised q * scale_t values) */
     const int32_t* head_slot;  /* [V]: row of term t in head_rows, or -1 */
-    const void* head_rows;     /* [n_head, head_ld], weight dtype */
+    const void* head_rows;     /* [n_head, head_ld], head_wdtype */
     int64_t head_ld;
 } gsp_index_view;
 
