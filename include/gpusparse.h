@@ -146,9 +146,12 @@ int64_t gsp_score_ws_bytes(const gsp_index_view* ix, int64_t B, int64_t W, int64
  * qs fp32 [B, W]) against every document, then the exact top-k per query:
  * out_scores fp32 [B, k'] descending, out_ids int64 [B, k'] global doc ids, with
  * k' = min(k, n_docs) and ties broken by ascending doc id.  Each document's score is
- * the fp32 sum of fl(q_w * d_w) over the query's (term id, slot) pairs in ascending
- * order, so results are bitwise reproducible.  Optionally also writes the packed
- * (score key << 32 | ~doc id) top-k to out_keys [B, k'] for a later gsp_merge_topk. */
+ * accumulated as acc = fma(q_w, d_w, acc) over the query's terms, head terms (those with
+ * dense rows) first, each group in ascending (term id, slot) order, so results are
+ * bitwise reproducible.  Optionally also writes the packed (score key << 32 | ~doc id)
+ * top-k to out_keys [B, k'] for a later gsp_merge_topk.  If an internal bounded wait
+ * ever ran out (it should not), the scores of that call are NaN and the ids -1.
+ * Replaces src/triton_kernel.py:159-200 (triton_fused_score). */
 int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const float* qs, int64_t B,
                    int64_t W, int64_t k, float* out_scores, int64_t* out_ids,
                    uint64_t* out_keys, void* ws, int64_t ws_bytes, void* stream);
@@ -157,8 +160,10 @@ int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const float* qs,
  * memory on the call path (a serving loop where cudaMalloc would synchronise the device,
  * or a host that gives the library only its input and output buffers).  No counterpart in
  * the reference.  Scratch is a fixed 32 MiB array compiled into the library, placed on
- * every GPU that loads it and held until exit; a batch whose plan and candidate buffers do
- * not fit (about B * k * 16 bytes plus the plan) is rejected with GSP_ERR_UNSUPPORTED.
+ * every GPU that loads it and held until exit.  The per-query candidate buffers shrink
+ * down to k + 2048 keys (more frequent compactions, same result); a batch that still does
+ * not fit (about B * (k + 2048) * 8 bytes plus the plan) is rejected with
+ * GSP_ERR_UNSUPPORTED.
  * Results equal gsp_score_topk's.  The first call on each device looks up the array's
  * device address (cudaGetSymbolAddress) with that device current; make that first call
  * before any stream capture.  All calls on a device share the one array: calls that
