@@ -211,6 +211,9 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
+        # rank 0 prints exactly one JSON line: keep NCCL's version banner off stdout
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
     wl = workload(args)
     N, B, k, wd = wl["num_docs"], wl["batch"], wl["k"], wl["wdtype"]

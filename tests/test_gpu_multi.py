@@ -1,0 +1,62 @@
+"""The sharded scorer as separate processes, one per GPU, over NCCL (skipped with fewer
+than two GPUs): every rank builds the index of its own document range with the global
+head set, and the all-gathered, merged top-k must equal the CPU oracle over the whole
+corpus bit for bit."""
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from parity import assert_bit_exact
+
+pytestmark = pytest.mark.gpu
+N, V, B, K = 30_000, 30522, 64, 1000
+
+
+def _free_port() -> int:
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=timedelta(seconds=120))
+    try:
+        from gpusparse import synth
+        from gpusparse.distributed import ShardLayout, global_head, sharded_score_topk
+        from gpusparse.index import N_HEAD, ensure_head
+        lay = ShardLayout(N, world, rank)
+        idx = synth.synth_index(N, V, seed=0, doc_range=(lay.lo, lay.hi), device=dev)
+        ensure_head(idx, head_ids=global_head(idx, N_HEAD))
+        qi, qs = synth.synth_queries(B, V, seed=1, device=dev)
+        s, i = sharded_score_topk(idx, lay, qi, qs, K)
+        torch.cuda.synchronize()
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), s=s.cpu().numpy(), i=i.cpu().numpy(),
+                 head=idx.head_ids.cpu().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_nccl_shards_equal_oracle(tmp_path):
+    import torch.multiprocessing as mp
+    world = 2
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    res = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
+    for r in range(1, world):                      # every rank holds the same result
+        assert np.array_equal(res[r]["s"], res[0]["s"]) and np.array_equal(res[r]["i"], res[0]["i"])
+        assert np.array_equal(res[r]["head"], res[0]["head"])
+    ip, ix, dt = O.synth_csr(N, V, seed=0)
+    qi, qs = O.synth_queries(B, V, seed=1)
+    rs, ri = O.score_topk(O.build_index(ip, ix, dt, V), qi, qs, K, head=res[0]["head"])
+    assert_bit_exact(res[0]["s"], res[0]["i"], rs, ri)
