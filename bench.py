@@ -211,9 +211,6 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        # rank 0 prints exactly one JSON line: keep NCCL's version banner off stdout
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
     wl = workload(args)
     N, B, k, wd = wl["num_docs"], wl["batch"], wl["k"], wl["wdtype"]
@@ -367,7 +364,7 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "clocks": clk,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_reference(args):
@@ -430,10 +427,24 @@ def run_reference(args):
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_JSON_FD = None
+
+
+def emit(line: dict) -> None:
+    """Write the one JSON result line to the process's original stdout."""
+    os.write(_JSON_FD if _JSON_FD is not None else 1, (json.dumps(line) + "\n").encode())
 
 
 def main():
+    global _JSON_FD
+    # Libraries (NCCL's version banner, for one) may print to stdout; everything but the
+    # result line goes to stderr so that stdout holds exactly one JSON line.
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     args = parse()
     if args.impl == "reference":
         run_reference(args)
