@@ -219,6 +219,48 @@ def ensure_head(index: GPUInvertedIndex, n_head: int = N_HEAD, head_ids=None) ->
     index.head_wdtype = code
 
 
+# ------------------------------------------------------------------ persistence
+# The reference rebuilds its index from the CSR on every run; a built index (posting
+# arrays, block rows and head rows) can be written once and loaded straight to a device.
+_FORMAT = "gpusparse-index-v1"
+_ARRAYS = ("doc_ids", "scores", "offsets", "lengths", "padded_lengths", "max_scores", "weights_q",
+           "term_scale", "block_starts", "head_ids", "head_slot", "head_rows")
+_SCALARS = ("num_docs", "vocab_size", "weight_dtype", "block_docs", "doc_base", "head_ld",
+            "head_wdtype")
+
+
+def save_index(index: GPUInvertedIndex, path) -> None:
+    """Write every array of a built index (with its block and head rows) to one file."""
+    ensure_blocks(index)
+    ensure_head(index)
+    state = {"format": _FORMAT}
+    for f in _SCALARS:
+        v = getattr(index, f)
+        state[f] = v if isinstance(v, str) else int(v)
+    state["arrays"] = {f: getattr(index, f).cpu() for f in _ARRAYS if getattr(index, f, None) is not None}
+    torch.save(state, path)
+
+
+def load_index(path, device) -> GPUInvertedIndex:
+    """Load an index written by save_index onto `device` (ValueError for other files)."""
+    device = _dev(device)
+    state = torch.load(path, map_location="cpu", weights_only=True)
+    if not isinstance(state, dict) or state.get("format") != _FORMAT:
+        raise ValueError(f"{path}: not a {_FORMAT} file")
+    arr = {f: t.to(device) for f, t in state["arrays"].items()}
+    idx = GPUInvertedIndex(doc_ids=arr["doc_ids"], scores=arr.get("scores"), offsets=arr["offsets"],
+                           lengths=arr["lengths"], padded_lengths=arr["padded_lengths"],
+                           max_scores=arr["max_scores"], num_docs=state["num_docs"],
+                           vocab_size=state["vocab_size"], device=device,
+                           weight_dtype=state["weight_dtype"], block_docs=state["block_docs"],
+                           doc_base=state["doc_base"])
+    for f in ("weights_q", "term_scale", "block_starts", "head_ids", "head_slot", "head_rows"):
+        setattr(idx, f, arr.get(f))
+    idx.head_ld = state["head_ld"]
+    idx.head_wdtype = state["head_wdtype"]
+    return idx
+
+
 def view(index: GPUInvertedIndex) -> L.IndexView:
     ensure_blocks(index)
     ensure_head(index)

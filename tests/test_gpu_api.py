@@ -165,3 +165,21 @@ def test_reference_style_index_with_repeated_doc_is_refused():
     qi, qs = O.synth_queries(4, 30522, seed=23)
     with pytest.raises(ValueError, match="repeat"):
         gpusparse.triton_fused_score(idx, t(qi), t(qs), top_k=10)
+
+
+@pytest.mark.parametrize("wd", ["fp32", "u8"])
+def test_index_save_load_round_trip(tmp_path, wd):
+    import gpusparse
+    ip, ix, dt = O.synth_csr(6000, 30522, seed=30)
+    g = gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), 30522, DEV, weight_dtype=wd)
+    qi, qs = O.synth_queries(20, 30522, seed=31)
+    a = gpusparse.triton_fused_score(g, t(qi), t(qs), top_k=500)
+    gpusparse.save_index(g, tmp_path / "index.pt")
+    h = gpusparse.load_index(tmp_path / "index.pt", DEV)
+    for f in ("doc_ids", "offsets", "lengths", "block_starts", "head_ids", "head_rows"):
+        assert torch.equal(getattr(h, f), getattr(g, f)), f
+    b = gpusparse.triton_fused_score(h, t(qi), t(qs), top_k=500)
+    assert torch.equal(a[1], b[1]) and torch.equal(a[0].view(torch.int32), b[0].view(torch.int32))
+    torch.save({"x": 1}, tmp_path / "other.pt")
+    with pytest.raises(ValueError):
+        gpusparse.load_index(tmp_path / "other.pt", DEV)
