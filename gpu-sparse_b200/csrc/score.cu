@@ -55,13 +55,21 @@ constexpr int kWarps = 8;
 #define GSP_SCORE_CTAS_PER_SM 4   // resident scoring CTAs per SM (register budget 65536 / (256 * this))
 #endif
 constexpr int kCtasPerSm = GSP_SCORE_CTAS_PER_SM;
-// with four CTAs per SM (64 registers) the head rows are summed in two halves of the tile,
-// with five or more in quarters, holding fewer accumulators and row values in registers
-constexpr int kHeadParts = kCtasPerSm >= 5 ? 4 : (kCtasPerSm >= 4 ? 2 : 1);
-constexpr int kHeadVec = 1024 / 128 / kHeadParts;   // float4 accumulators per lane per part
 constexpr int kPlanThreads = 256;
 constexpr int kMaxWidth = 4096;   // query slots (W) supported
-constexpr int kTile = 1024;       // documents per tile = index block
+constexpr int kBlock = 1024;      // documents per index block (block_starts row)
+#ifndef GSP_TILE_BLOCKS
+#define GSP_TILE_BLOCKS 1         // index blocks per scoring tile
+#endif
+constexpr int kTile = kBlock * GSP_TILE_BLOCKS;   // documents per scoring tile
+constexpr int kSel = 1024;        // documents one selection pass marks (32 per lane)
+constexpr int kTileBlocksI = GSP_TILE_BLOCKS;
+// the head rows are summed over parts of the tile, 1024 documents each with 80 registers
+// (three CTAs per SM), 512 with 64 (four), 256 with fewer, so that the accumulators and
+// row values of one part fit in registers
+constexpr int kHeadPart = kCtasPerSm >= 5 ? 256 : (kCtasPerSm >= 4 ? 512 : 1024);
+constexpr int kHeadParts = kTile / kHeadPart;
+constexpr int kHeadVec = kHeadPart / 128;   // float4 accumulators per lane per part
 constexpr int kLongRun = 48;      // tail windows at least this long are streamed on their own
 constexpr int kSpinLimit = 1 << 21;   // polls of a bounded wait (about a second)
 constexpr int kCompactUnroll = 8;     // keys per lane loaded together by a compaction pass
@@ -78,12 +86,13 @@ struct ScoreParams {
   int64_t n_docs;
   int64_t doc_base;
   int32_t V;
-  int32_t n_blocks;
+  int32_t n_blocks;     // scoring tiles
+  int32_t n_iblocks;    // index blocks (block_starts has n_iblocks + 1 rows)
   int32_t B;
   int32_t k;
   int32_t ecap;      // plan capacity per query (= W)
   int32_t cap;       // candidate buffer capacity per query (keys), > k
-  int64_t cand_stride;   // keys per query buffer: cap + kTile spare slots for the crossing warp
+  int64_t cand_stride;   // keys per query buffer: cap + kSel spare slots for the crossing warp
   // plan, per query: head entries and tail runs
   const int32_t* n_head_e;
   const uint16_t* head_h;
@@ -430,7 +439,7 @@ __device__ __forceinline__ uint32_t mark_tile(const float* __restrict__ acc, int
   const float ts = thi < 0x00800000u ? -INFINITY : fkey_inv(thi);
   uint32_t m = 0;
 #pragma unroll
-  for (int i = 0; i < kTile / 128; ++i) {
+  for (int i = 0; i < kSel / 128; ++i) {
     const float4 v = *reinterpret_cast<const float4*>(acc + 128 * i + 4 * lane);
     const uint32_t c = uint32_t(128 * i + 4 * lane);
     m |= uint32_t(c < span && v.x >= ts) << (4 * i);
@@ -614,7 +623,9 @@ score_kernel(const ScoreParams p) {
       const unsigned long long g_pub = __ldcg(p.gthr + q);   // consumed by the selection
 
       // 2. tail runs in ascending term id
-      const uint32_t* __restrict__ brow = p.block_starts + int64_t(b) * p.V;
+      const uint32_t* __restrict__ brow = p.block_starts + int64_t(b) * kTileBlocksI * p.V;
+      const uint32_t* __restrict__ brow_end =
+          p.block_starts + int64_t(min((b + 1) * kTileBlocksI, p.n_iblocks)) * p.V;
       for (int32_t rb = 0; rb < nr; rb += 32) {
         const int32_t ri = rb + lane;
         uint32_t lo = 0, hi = 0, b32 = 0;
@@ -623,7 +634,7 @@ score_kernel(const ScoreParams p) {
         if (ri < nr) {
           const int32_t t = run_term[ri];
           lo = __ldg(brow + t);
-          hi = __ldg(brow + p.V + t);
+          hi = __ldg(brow_end + t);
           e0 = ri ? int32_t(run_end[ri - 1]) : 0;
           ne = int32_t(run_end[ri]) - e0;
           b32 = run_b32[ri];
@@ -712,11 +723,16 @@ score_kernel(const ScoreParams p) {
       // its candidate buffer (a superset of the keys >= threshold is harmless: only the k
       // largest survive the compactions and the merge)
       const uint64_t thr = uint64_t(g_pub);
-      const uint32_t m = mark_tile(acc, lane, span, thr);
-      if (__any_sync(FULL, m != 0u)) {
-        QueryBuf qb{p.cand + int64_t(q) * p.cand_stride, p.gthr + q, p.resv + q, p.done + q, p.gen + q,
-                    p.fault, p.cap, p.k};
-        append_candidates(qb, acc, span, uint32_t(p.doc_base + d0i), hist, thr, m);
+#pragma unroll
+      for (int h = 0; h < kTile / kSel; ++h) {
+        if (uint32_t(h * kSel) >= span) break;
+        const uint32_t sp = min(span - uint32_t(h * kSel), uint32_t(kSel));
+        const uint32_t m = mark_tile(acc + h * kSel, lane, sp, thr);
+        if (__any_sync(FULL, m != 0u)) {
+          QueryBuf qb{p.cand + int64_t(q) * p.cand_stride, p.gthr + q, p.resv + q, p.done + q, p.gen + q,
+                      p.fault, p.cap, p.k};
+          append_candidates(qb, acc + h * kSel, sp, uint32_t(p.doc_base + d0i + h * kSel), hist, thr, m);
+        }
       }
     }
   }
@@ -724,7 +740,7 @@ score_kernel(const ScoreParams p) {
 
 struct Cfg {
   int npow2 = 0, cap = 0, smem = 0, ctas_per_sm = 0, grid = 0;
-  int64_t ecap = 0, n_blocks = 0, kk = 0, stride = 0;
+  int64_t ecap = 0, n_blocks = 0, n_iblocks = 0, kk = 0, stride = 0;
   int64_t off_nhe = 0, off_hh = 0, off_hw = 0, off_hs = 0, off_nruns = 0, off_rterm = 0, off_rb32 = 0,
           off_rend = 0, off_rw0 = 0, off_entw = 0, off_cand = 0, off_zero = 0, zero_bytes = 0, total = 0;
 };
@@ -736,7 +752,7 @@ int64_t align8(int64_t x) { return (x + 7) / 8 * 8; }
 void set_layout(Cfg& c, int64_t B) {
   int64_t o = 0;
   const int64_t E = B * c.ecap;
-  c.stride = c.cap + kTile;
+  c.stride = c.cap + kSel;
   c.off_nhe = o; o = align256(o + B * 4);
   c.off_hh = o; o = align256(o + E * 2);
   c.off_hw = o; o = align256(o + E * 4);
@@ -757,8 +773,8 @@ void set_layout(Cfg& c, int64_t B) {
 int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) {
   GSP_REQUIRE(ix && ix->V > 0 && ix->n_docs >= 0 && ix->block_docs > 0, GSP_ERR_ARG,
               "score: bad index view");
-  GSP_REQUIRE(ix->block_docs == kTile, GSP_ERR_UNSUPPORTED,
-              "score: the scorer needs index blocks of %d documents (this index has %d)", kTile,
+  GSP_REQUIRE(ix->block_docs == kBlock, GSP_ERR_UNSUPPORTED,
+              "score: the scorer needs index blocks of %d documents (this index has %d)", kBlock,
               ix->block_docs);
   GSP_REQUIRE(B >= 0 && W >= 1 && k >= 1, GSP_ERR_ARG, "score: bad batch shape (B=%lld W=%lld k=%lld)",
               (long long)B, (long long)W, (long long)k);
@@ -776,11 +792,12 @@ int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) 
   c.npow2 = kPlanThreads;
   while (c.npow2 < W) c.npow2 <<= 1;
   c.n_blocks = (ix->n_docs + kTile - 1) / kTile;
+  c.n_iblocks = (ix->n_docs + kBlock - 1) / kBlock;
   // one persistent CTA per resident slot; fewer when the batch has fewer items
   const int64_t items = B * c.n_blocks;
   c.grid = int(std::max<int64_t>(1, std::min<int64_t>(int64_t(sms) * c.ctas_per_sm, (items + kWarps - 1) / kWarps)));
   // a compaction keeps k keys; the rest of the capacity takes several tiles' candidates
-  c.cap = int(((std::max<int64_t>(4 * c.kk, c.kk + 4 * kTile) + 31) / 32) * 32);
+  c.cap = int(((std::max<int64_t>(4 * c.kk, c.kk + 4 * kSel) + 31) / 32) * 32);
   set_layout(c, B);
   return GSP_OK;
 }
@@ -863,6 +880,7 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.doc_base = ix->doc_base;
   p.V = ix->V;
   p.n_blocks = int32_t(c.n_blocks);
+  p.n_iblocks = int32_t(c.n_iblocks);
   p.B = int32_t(B);
   p.k = int32_t(c.kk);
   p.ecap = int32_t(c.ecap);
@@ -1000,7 +1018,7 @@ extern "C" int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* q
   // count, only the parallelism does
   // a smaller candidate capacity means more frequent compactions, never another result;
   // the smallest one keeps k keys plus a whole tile
-  const int min_cap = int(((c.kk + kTile + 31) / 32) * 32);
+  const int min_cap = int(((c.kk + kSel + 31) / 32) * 32);
   while (c.total > int64_t(kNoAllocScratchBytes) && c.cap > min_cap) {
     c.cap = std::max(min_cap, c.cap / 2 / 32 * 32);
     set_layout(c, B);

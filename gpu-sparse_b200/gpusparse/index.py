@@ -31,6 +31,7 @@ from . import _lib as L
 BLOCK_SIZE = 32          # posting lists are padded to a warp (src/gpu_inverted_index.py:18)
 BLOCK_DOCS = 1024        # documents per block_starts row = the scorer's document tile
 N_HEAD = 128             # densest terms scored from dense rows instead of posting lists
+HEAD_PAD = 4096          # head rows cover a multiple of this many documents
 VOCAB_SIZE = 30522       # src/run_correctness_verification.py:28
 
 
@@ -185,8 +186,8 @@ def ensure_head(index: GPUInvertedIndex, n_head: int = N_HEAD, head_ids=None) ->
         return
     dev = index.device
     V = int(index.vocab_size)
-    bd = getattr(index, "block_docs", None) or BLOCK_DOCS
-    ld = ((int(index.num_docs) + bd - 1) // bd) * bd
+    # rows padded to a multiple of HEAD_PAD documents, whole scoring tiles
+    ld = ((int(index.num_docs) + HEAD_PAD - 1) // HEAD_PAD) * HEAD_PAD
     H = min(int(n_head), V)
     lengths = index.lengths
     H = min(H, int((lengths > 0).sum().item()))
