@@ -11,14 +11,16 @@
 // no search.  The warp owns the tile's fp32 accumulators, so every (query, document) cell
 // has exactly one writer, and the result does not depend on which warp scored which item.
 //
-// Candidates.  Each query has one candidate buffer shared by all warps, with a
-// reservation counter (resv), a written counter (done) and a generation.  A warp reserves
-// room for its keys with one atomicAdd; below the capacity it writes them and adds their
-// count to done.  The warp whose reservation crosses the capacity writes its keys into the
-// buffer's spare tail, waits until done reaches its reservation (every earlier writer has
-// finished), keeps the k largest keys, publishes the k-th as the query's threshold and
-// reopens the buffer (done = resv = k, generation + 1).  Warps that reserved past the
-// capacity wait for the generation to change and retry against the raised threshold.
+// Candidates.  Each query has one candidate buffer shared by all warps, with a 64-bit
+// reservation word (generation << 32 | reserved slots) and a written counter (done).  A
+// warp reserves room for its keys with one atomicAdd on the word, which also tells it the
+// generation its reservation belongs to; below the capacity it writes the keys and adds
+// their count to done.  The warp whose reservation crosses the capacity writes its keys
+// into the buffer's spare tail, waits until done reaches its reservation (every earlier
+// writer has finished), keeps the k largest keys, publishes the k-th as the query's
+// threshold and reopens the buffer (done = k, then the word = (generation + 1, k) in one
+// exchange).  Warps that reserved past the capacity wait for the word's generation to
+// change and retry against the raised threshold.
 // Every wait is bounded; one that runs out records a fault, and the merge then reports
 // NaN scores instead of a result.
 //
@@ -106,9 +108,8 @@ struct ScoreParams {
   const float* ent_w;
   uint64_t* cand;              // [B, cand_stride]
   unsigned long long* gthr;    // [B] published lower bound of each query's k-th key (zeroed)
-  int32_t* resv;               // [B] reserved slots (zeroed)
+  unsigned long long* rg;      // [B] generation << 32 | reserved slots (zeroed)
   int32_t* done;               // [B] written slots (zeroed); final candidate counts
-  uint32_t* gen;               // [B] buffer generation (zeroed)
   unsigned long long* item_next;   // next work item (zeroed)
   int32_t* fault;              // a bounded wait ran out (zeroed)
 };
@@ -469,9 +470,9 @@ __device__ __forceinline__ bool wait_equal(const int32_t* a, int32_t v) {
   }
   return false;
 }
-__device__ __forceinline__ bool wait_change(const uint32_t* a, uint32_t v) {
+__device__ __forceinline__ bool wait_generation(const unsigned long long* a, uint32_t g) {
   for (int i = 0; i < kSpinLimit; ++i) {
-    if (*reinterpret_cast<const volatile uint32_t*>(a) != v) return true;
+    if (uint32_t(*reinterpret_cast<const volatile unsigned long long*>(a) >> 32) != g) return true;
     __nanosleep(64);
   }
   return false;
@@ -481,9 +482,8 @@ __device__ __forceinline__ bool wait_change(const uint32_t* a, uint32_t v) {
 struct QueryBuf {
   uint64_t* buf;
   unsigned long long* gthr;
-  int32_t* resv;
+  unsigned long long* rg;
   int32_t* done;
-  uint32_t* gen;
   int32_t* fault;
   int32_t cap, k;
 };
@@ -502,14 +502,12 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
     const int32_t incl = lane_scan(cnt);
     const int32_t total = __shfl_sync(FULL, incl, 31);
     if (total == 0) return;
-    uint32_t g0 = 0;
-    int32_t pos = 0;
-    if (lane == 0) {
-      g0 = *reinterpret_cast<const volatile uint32_t*>(qb.gen);
-      pos = atomicAdd(qb.resv, total);
-    }
-    g0 = __shfl_sync(FULL, g0, 0);
-    pos = __shfl_sync(FULL, pos, 0);
+    // one atomic gives the reservation and the generation it belongs to
+    unsigned long long word = 0;
+    if (lane == 0) word = atomicAdd(qb.rg, (unsigned long long)total);
+    word = __shfl_sync(FULL, word, 0);
+    const int32_t pos = int32_t(uint32_t(word));
+    const uint32_t g0 = uint32_t(word >> 32);
     if (pos <= qb.cap) {
       // below the capacity: write the keys (a crossing reservation runs into the spare tail)
       int32_t o = pos + incl - cnt;
@@ -538,9 +536,7 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
         atomicMax(qb.gthr, (unsigned long long)t);
         atomicExch(qb.done, qb.k);
         __threadfence();
-        atomicExch(qb.resv, qb.k);
-        __threadfence();
-        atomicAdd(qb.gen, 1u);
+        atomicExch(qb.rg, (static_cast<unsigned long long>(g0 + 1u) << 32) | uint32_t(qb.k));
       }
       __syncwarp();
       return;
@@ -548,7 +544,7 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
     // another warp is compacting: wait for the buffer to reopen, then retry against the
     // raised threshold
     bool ok = true;
-    if (lane == 0) ok = wait_change(qb.gen, g0);
+    if (lane == 0) ok = wait_generation(qb.rg, g0);
     ok = __shfl_sync(FULL, int(ok), 0) != 0;
     if (!ok) {
       if (lane == 0) atomicOr(qb.fault, 1);
@@ -729,8 +725,8 @@ score_kernel(const ScoreParams p) {
         const uint32_t sp = min(span - uint32_t(h * kSel), uint32_t(kSel));
         const uint32_t m = mark_tile(acc + h * kSel, lane, sp, thr);
         if (__any_sync(FULL, m != 0u)) {
-          QueryBuf qb{p.cand + int64_t(q) * p.cand_stride, p.gthr + q, p.resv + q, p.done + q, p.gen + q,
-                      p.fault, p.cap, p.k};
+          QueryBuf qb{p.cand + int64_t(q) * p.cand_stride, p.gthr + q, p.rg + q, p.done + q, p.fault,
+                      p.cap, p.k};
           append_candidates(qb, acc + h * kSel, sp, uint32_t(p.doc_base + d0i + h * kSel), hist, thr, m);
         }
       }
@@ -764,9 +760,9 @@ void set_layout(Cfg& c, int64_t B) {
   c.off_rw0 = o; o = align256(o + E * 4);
   c.off_entw = o; o = align256(o + E * 4);
   c.off_cand = o; o = align256(o + B * c.stride * 8);
-  // cleared by every call: thresholds [B] u64, resv [B], done [B], generation [B],
+  // cleared by every call: thresholds [B] u64, reservation words [B] u64, done [B],
   // item counter u64, fault flag
-  c.off_zero = o; c.zero_bytes = align8(B * 8 + 3 * B * 4) + 16; o = align256(o + c.zero_bytes);
+  c.off_zero = o; c.zero_bytes = align8(2 * B * 8 + B * 4) + 16; o = align256(o + c.zero_bytes);
   c.total = o;
 }
 
@@ -899,10 +895,9 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.cand = reinterpret_cast<uint64_t*>(w + c.off_cand);
   char* z = w + c.off_zero;
   p.gthr = reinterpret_cast<unsigned long long*>(z);
-  p.resv = reinterpret_cast<int32_t*>(z + B * 8);
-  p.done = p.resv + B;
-  p.gen = reinterpret_cast<uint32_t*>(p.done + B);
-  p.item_next = reinterpret_cast<unsigned long long*>(z + align8(B * 8 + 3 * B * 4));
+  p.rg = reinterpret_cast<unsigned long long*>(z + B * 8);
+  p.done = reinterpret_cast<int32_t*>(z + 2 * B * 8);
+  p.item_next = reinterpret_cast<unsigned long long*>(z + align8(2 * B * 8 + B * 4));
   p.fault = reinterpret_cast<int32_t*>(p.item_next + 1);
   GSP_CUDA(cudaMemsetAsync(z, 0, size_t(c.zero_bytes), st));
 

@@ -86,7 +86,8 @@ def to_query_tensors(q_csr, device):
 
 def retrieve(index, q_ids, q_ti, q_ts, doc_ids, k, batch_size=200, doc_chunk=131072):
     """Score in batches of `batch_size`; per query the top-k (query id, score, doc id)
-    triples with score > 0, best first (reference :135-172)."""
+    triples with score > 0, best first (reference :135-172).  The next batch is scored
+    on the GPU while the host turns the previous one into Python lists."""
     results = []
     n = q_ti.shape[0]
     kk = min(k, index.num_docs)
@@ -94,8 +95,8 @@ def retrieve(index, q_ids, q_ti, q_ts, doc_ids, k, batch_size=200, doc_chunk=131
     bounds = build_chunk_boundaries(index, doc_chunk) if chunked else None
     doc_ids_arr = np.asarray(doc_ids, dtype=object)
     pin = torch.cuda.is_available()
-    for s0 in range(0, n, batch_size):
-        s1 = min(s0 + batch_size, n)
+
+    def launch(s0, s1):
         qi = q_ti[s0:s1].contiguous()
         qs = q_ts[s0:s1].contiguous()
         if chunked:
@@ -107,7 +108,13 @@ def retrieve(index, q_ids, q_ti, q_ts, doc_ids, k, batch_size=200, doc_chunk=131
         hi = torch.empty(ids.shape, dtype=ids.dtype, pin_memory=pin)
         hs.copy_(scores, non_blocking=True)
         hi.copy_(ids, non_blocking=True)
-        torch.cuda.current_stream(scores.device).synchronize()
+        done = torch.cuda.Event()
+        done.record(torch.cuda.current_stream(scores.device))
+        return s0, s1, hs, hi, done
+
+    def collect(batch):
+        s0, s1, hs, hi, done = batch
+        done.synchronize()
         hs, hi = hs.numpy(), hi.numpy()
         for r in range(s1 - s0):
             keep = hs[r] > 0
@@ -115,6 +122,15 @@ def retrieve(index, q_ids, q_ti, q_ts, doc_ids, k, batch_size=200, doc_chunk=131
             dn = doc_ids_arr[hi[r][keep]].tolist()
             qid = q_ids[s0 + r]
             results.append([(qid, s, d) for s, d in zip(sc, dn)])
+
+    pending = None
+    for s0 in range(0, n, batch_size):
+        batch = launch(s0, min(s0 + batch_size, n))
+        if pending is not None:
+            collect(pending)
+        pending = batch
+    if pending is not None:
+        collect(pending)
     return results
 
 
