@@ -44,6 +44,7 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <stdio.h>
 #include <stdlib.h>
@@ -73,7 +74,7 @@ constexpr int kHeadPart = kCtasPerSm >= 5 ? 256 : (kCtasPerSm >= 4 ? 512 : 1024)
 constexpr int kHeadParts = kTile / kHeadPart;
 constexpr int kHeadVec = kHeadPart / 128;   // float4 accumulators per lane per part
 constexpr int kLongRun = 48;      // tail windows at least this long are streamed on their own
-constexpr int kSpinLimit = 1 << 21;   // polls of a bounded wait (about a second)
+constexpr int kSpinLimit = 1 << 21;   // default polls of a bounded wait (about a second)
 constexpr int kCompactUnroll = 8;     // keys per lane loaded together by a compaction pass
 
 struct ScoreParams {
@@ -112,6 +113,7 @@ struct ScoreParams {
   int32_t* done;               // [B] written slots (zeroed); final candidate counts
   unsigned long long* item_next;   // next work item (zeroed)
   int32_t* fault;              // a bounded wait ran out (zeroed)
+  int32_t wait_limit;          // polls before a wait gives up
 };
 
 namespace {
@@ -463,15 +465,15 @@ __device__ __forceinline__ int32_t lane_scan(int32_t x) {
 }
 
 // Bounded polls of a word that other warps of this launch update (read through L2).
-__device__ __forceinline__ bool wait_equal(const int32_t* a, int32_t v) {
-  for (int i = 0; i < kSpinLimit; ++i) {
+__device__ __forceinline__ bool wait_equal(const int32_t* a, int32_t v, int32_t limit) {
+  for (int i = 0; i < limit; ++i) {
     if (*reinterpret_cast<const volatile int32_t*>(a) == v) return true;
     __nanosleep(64);
   }
   return false;
 }
-__device__ __forceinline__ bool wait_generation(const unsigned long long* a, uint32_t g) {
-  for (int i = 0; i < kSpinLimit; ++i) {
+__device__ __forceinline__ bool wait_generation(const unsigned long long* a, uint32_t g, int32_t limit) {
+  for (int i = 0; i < limit; ++i) {
     if (uint32_t(*reinterpret_cast<const volatile unsigned long long*>(a) >> 32) != g) return true;
     __nanosleep(64);
   }
@@ -486,6 +488,7 @@ struct QueryBuf {
   int32_t* done;
   int32_t* fault;
   int32_t cap, k;
+  int32_t wait_limit;
 };
 
 // Appends the tile's documents whose score reaches threshold key thr (marked in m) to a
@@ -526,7 +529,7 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
       // this warp crossed the capacity: once every earlier reservation is written, keep
       // the k largest keys, publish the k-th as the threshold and reopen the buffer
       bool ok = true;
-      if (lane == 0) ok = wait_equal(qb.done, pos);
+      if (lane == 0) ok = wait_equal(qb.done, pos, qb.wait_limit);
       ok = __shfl_sync(FULL, int(ok), 0) != 0;
       if (!ok && lane == 0) atomicOr(qb.fault, 1);
       __threadfence();
@@ -544,7 +547,7 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
     // another warp is compacting: wait for the buffer to reopen, then retry against the
     // raised threshold
     bool ok = true;
-    if (lane == 0) ok = wait_generation(qb.rg, g0);
+    if (lane == 0) ok = wait_generation(qb.rg, g0, qb.wait_limit);
     ok = __shfl_sync(FULL, int(ok), 0) != 0;
     if (!ok) {
       if (lane == 0) atomicOr(qb.fault, 1);
@@ -726,7 +729,7 @@ score_kernel(const ScoreParams p) {
         const uint32_t m = mark_tile(acc + h * kSel, lane, sp, thr);
         if (__any_sync(FULL, m != 0u)) {
           QueryBuf qb{p.cand + int64_t(q) * p.cand_stride, p.gthr + q, p.rg + q, p.done + q, p.fault,
-                      p.cap, p.k};
+                      p.cap, p.k, p.wait_limit};
           append_candidates(qb, acc + h * kSel, sp, uint32_t(p.doc_base + d0i + h * kSel), hist, thr, m);
         }
       }
@@ -742,6 +745,7 @@ struct Cfg {
 };
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+std::atomic<int32_t> g_wait_limit{kSpinLimit};
 int64_t align8(int64_t x) { return (x + 7) / 8 * 8; }
 
 // Workspace layout of one call for the configured buffer capacity.
@@ -881,6 +885,7 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.k = int32_t(c.kk);
   p.ecap = int32_t(c.ecap);
   p.cap = c.cap;
+  p.wait_limit = g_wait_limit.load();
   p.cand_stride = c.stride;
   p.n_head_e = reinterpret_cast<int32_t*>(w + c.off_nhe);
   p.head_h = reinterpret_cast<uint16_t*>(w + c.off_hh);
@@ -927,6 +932,14 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   return merge_topk_device(p.cand, B, 1, c.stride, 0, p.done, 1, nullptr, c.kk, out_scores, out_ids,
                            out_keys, st, -1, p.fault);
 }
+
+extern "C" int gsp_set_wait_limit(int32_t polls) {
+  GSP_REQUIRE(polls >= 0, GSP_ERR_ARG, "gsp_set_wait_limit: negative limit");
+  g_wait_limit.store(polls);
+  return GSP_OK;
+}
+
+extern "C" int32_t gsp_get_wait_limit(void) { return g_wait_limit.load(); }
 
 extern "C" int gsp_profile_enable(int on) {
   Profile& pr = profile();

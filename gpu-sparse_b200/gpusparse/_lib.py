@@ -31,7 +31,7 @@ EXPORTS = (
     "gsp_last_error", "gsp_version", "gsp_scan_i32", "gsp_scan_ws_bytes", "gsp_synth_nnz",
     "gsp_synth_fill", "gsp_index_ws_bytes", "gsp_index_count", "gsp_index_fill",
     "gsp_index_quantize", "gsp_index_head_rows", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
-    "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_profile_enable", "gsp_profile_collect", "gsp_merge_topk",
+    "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_merge_topk",
     "gsp_compacted_ws_bytes", "gsp_compacted_topk",
 )
 
@@ -94,6 +94,8 @@ def lib() -> ctypes.CDLL:
             "gsp_score_topk_noalloc": (ctypes.c_int, [ctypes.POINTER(IndexView), p, p, i64, i64,
                                                       i64, p, p, p, p]),
             "gsp_profile_enable": (ctypes.c_int, [ctypes.c_int]),
+            "gsp_set_wait_limit": (ctypes.c_int, [ctypes.c_int32]),
+            "gsp_get_wait_limit": (ctypes.c_int32, []),
             "gsp_profile_collect": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double),
                                                    ctypes.POINTER(i64)]),
             "gsp_merge_topk": (ctypes.c_int, [p, i64, i64, i64, i64, p, i64, p, p, p, p]),

@@ -177,6 +177,14 @@ int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* qi, const fl
  * launch with CUDA events on the caller's stream; collect synchronises on them and returns
  * the summed duration and the number of launches, then resets.  One device per process. */
 int gsp_profile_enable(int on);
+
+/* Polls a scoring call's bounded waits make before giving up (no reference counterpart;
+ * a diagnostic control, default 2^21, about a second).  A wait that gives up records a
+ * fault and that call returns NaN scores and ids -1 instead of a result; the context stays
+ * usable.  0 makes every wait give up at once (tests use it to exercise that path).
+ * Applies to calls issued after it; process-wide. */
+int gsp_set_wait_limit(int32_t polls);
+int32_t gsp_get_wait_limit(void);
 int gsp_profile_collect(double* total_ms, int64_t* launches);
 
 /* ---------------------------------------------------------------- selection */
