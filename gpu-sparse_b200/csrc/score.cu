@@ -81,8 +81,6 @@ struct ScoreParams {
   const int32_t* doc_ids;
   const void* weights;
   const float* term_scale;
-  const int64_t* offsets;
-  const int32_t* lengths;
   const uint32_t* block_starts;
   const void* head_rows;
   int64_t head_ld;
@@ -871,8 +869,6 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.doc_ids = ix->doc_ids;
   p.weights = ix->weights;
   p.term_scale = ix->term_scale;
-  p.offsets = ix->offsets;
-  p.lengths = ix->lengths;
   p.block_starts = ix->block_starts;
   p.head_rows = ix->head_rows;
   p.head_ld = ix->head_ld;

@@ -4,11 +4,12 @@
 // better (higher score, then lower doc id), and keys of one query are distinct, so "the k
 // largest keys" is exactly the reference's top-k with deterministic tie-breaking.
 //
-// merge_kernel: one CTA per query.  Radix-select the k-th largest key over the query's
-// candidate lists (R per query, or a ragged range of lists per query) (8-bit digits, most significant first, shared-memory histogram with
+// merge_kernel: one CTA per query.  Radix-select the k-th largest key over the query's R
+// candidate lists (8-bit digits, most significant first, shared-memory histogram with
 // warp-aggregated increments, early exit once the boundary bucket is taken whole), gather
 // the k keys at or above the boundary into shared memory, bitonic-sort them descending
-// and decode (score, doc id).  This replaces torch.topk over the dense matrix
+// and decode (score, doc id).  If the producer of the candidates reported a fault, the
+// query's output is NaN scores and ids -1 instead.  This replaces torch.topk over the dense matrix
 // (src/triton_kernel.py:199), the running cat/topk/gather merge
 // (src/triton_kernel_chunked.py:162-168) and the host-side shard merge
 // (src/comprehensive_benchmark.py:472-480).
