@@ -38,3 +38,30 @@ def test_contended_buffers_are_exact_and_repeatable(big, B):
         rs, ri = O.score_topk(oidx, qi.cpu().numpy(), qs.cpu().numpy(), 1000,
                               head=index.head_ids.cpu().numpy())
         assert_bit_exact(runs[0][0].cpu().numpy(), runs[0][1].cpu().numpy(), rs, ri)
+
+
+def test_layout_invariant_at_scale(big):
+    """Every list of a 1M-document build ascends strictly (the reference's run_invariant)."""
+    import ctypes
+    import gpusparse._lib as L
+    index, _ = big
+    bad, dup = ctypes.c_int64(-1), ctypes.c_int64(-1)
+    L.check(L.lib().gsp_check_sorted(V, L.ptr(index.doc_ids), L.ptr(index.offsets), L.ptr(index.lengths),
+                                     ctypes.byref(bad), ctypes.byref(dup), L.stream_of(DEV)), "check")
+    assert bad.value == 0 and dup.value == 0
+
+
+def test_batch_times_documents_beyond_2_31(big):
+    """2500 queries x 1M documents = 2.5e9 (query, document) cells: no 32-bit index wraps
+    (the reference guards B * N > 2^31 with int64 index math)."""
+    import gpusparse
+    from gpusparse import synth
+    index, (ip, ix, dt) = big
+    qi, qs = synth.synth_queries(2500, V, seed=6, device=DEV)
+    s, i = gpusparse.triton_fused_score(index, qi, qs, top_k=100)
+    assert not torch.isnan(s).any()
+    rows = [0, 1, 1249, 2498, 2499]
+    oidx = O.build_index(ip, ix, dt, V)
+    rs, ri = O.score_topk(oidx, qi[rows].cpu().numpy(), qs[rows].cpu().numpy(), 100,
+                          head=index.head_ids.cpu().numpy())
+    assert_bit_exact(s[rows].cpu().numpy(), i[rows].cpu().numpy(), rs, ri)
