@@ -11,16 +11,19 @@
 // no search.  The warp owns the tile's fp32 accumulators, so every (query, document) cell
 // has exactly one writer, and the result does not depend on which warp scored which item.
 //
-// Candidates.  Each query has one candidate buffer shared by all warps, with a 64-bit
-// reservation word (generation << 32 | reserved slots) and a written counter (done).  A
-// warp reserves room for its keys with one atomicAdd on the word, which also tells it the
-// generation its reservation belongs to; below the capacity it writes the keys and adds
-// their count to done.  The warp whose reservation crosses the capacity writes its keys
-// into the buffer's spare tail, waits until done reaches its reservation (every earlier
-// writer has finished), keeps the k largest keys, publishes the k-th as the query's
-// threshold and reopens the buffer (done = k, then the word = (generation + 1, k) in one
-// exchange).  Warps that reserved past the capacity wait for the word's generation to
-// change and retry against the raised threshold.
+// Candidates.  Each query has two candidate buffers used in turn and a keep list of the k
+// best keys found so far, shared by all warps; a 64-bit word (generation << 32 | reserved
+// slots) says which buffer is open (the generation's low bit) and how far it is reserved,
+// and a written counter per buffer counts finished writes.  A warp reserves room for its
+// keys with one atomicAdd on the word, which also tells it the generation; below the
+// capacity it writes the keys and adds their count to the buffer's written counter.  The
+// warp whose reservation crosses the capacity writes its keys into the buffer's spare
+// tail, waits for the previous compaction to finish (it read the other buffer and wrote
+// the keep list), opens the next generation on the other buffer, empty, so that the other
+// warps go on appending there, waits until every earlier reservation of its own
+// generation is written, and then keeps the k largest of that buffer and the keep list as
+// the new keep list and publishes the k-th as the query's threshold.  Warps that reserved
+// past the capacity wait only until the next generation is open.
 // Every wait is bounded; one that runs out records a fault, and the merge then reports
 // NaN scores instead of a result.
 //
@@ -93,7 +96,7 @@ struct ScoreParams {
   int32_t k;
   int32_t ecap;      // plan capacity per query (= W)
   int32_t cap;       // candidate buffer capacity per query (keys), > k
-  int64_t cand_stride;   // keys per query buffer: cap + kSel spare slots for the crossing warp
+  int64_t cand_stride;   // keys per buffer: cap + kSel (the crossing warp's spare tail) + k (the keep list, for a compaction)
   // plan, per query: head entries and tail runs
   const int32_t* n_head_e;
   const uint16_t* head_h;
@@ -105,10 +108,12 @@ struct ScoreParams {
   const uint16_t* run_end;
   const float* run_w0;
   const float* ent_w;
-  uint64_t* cand;              // [B, cand_stride]
+  uint64_t* cand;              // [B, 3, cand_stride]: keep list, buffer 0, buffer 1
   unsigned long long* gthr;    // [B] published lower bound of each query's k-th key (zeroed)
   unsigned long long* rg;      // [B] generation << 32 | reserved slots (zeroed)
-  int32_t* done;               // [B] written slots (zeroed); final candidate counts
+  int32_t* done;               // [B, 2] written slots per buffer (zeroed)
+  int32_t* cdone;              // [B] finished compactions (zeroed)
+  int32_t* counts;             // [B, 3] final candidates: keep list, buffer 0, buffer 1
   unsigned long long* item_next;   // next work item (zeroed)
   int32_t* fault;              // a bounded wait ran out (zeroed)
   int32_t wait_limit;          // polls before a wait gives up
@@ -480,23 +485,24 @@ __device__ __forceinline__ bool wait_generation(const unsigned long long* a, uin
 
 // Per-query state of the shared candidate buffers.
 struct QueryBuf {
-  uint64_t* buf;
+  uint64_t* region;            // keep list, buffer 0, buffer 1, stride keys apart
+  int64_t stride;
   unsigned long long* gthr;
   unsigned long long* rg;
-  int32_t* done;
+  int32_t* done;               // [2]
+  int32_t* cdone;
   int32_t* fault;
   int32_t cap, k;
   int32_t wait_limit;
 };
 
 // Appends the tile's documents whose score reaches threshold key thr (marked in m) to a
-// query's shared candidate buffer, following the reservation protocol described at the
-// top of the file.  Called only for tiles with a candidate.
+// query's candidate buffers, following the protocol described at the top of the file.
+// Called only for tiles with a candidate.
 __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restrict__ acc, uint32_t span,
                                                uint32_t dbase, uint32_t* __restrict__ hist, uint64_t thr,
                                                uint32_t m) {
   const int lane = lane_id();
-  uint64_t* __restrict__ buf = qb.buf;
   for (bool first = true;; first = false) {
     if (!first) m = mark_tile(acc, lane, span, thr);
     const int32_t cnt = __popc(m);
@@ -509,6 +515,8 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
     word = __shfl_sync(FULL, word, 0);
     const int32_t pos = int32_t(uint32_t(word));
     const uint32_t g0 = uint32_t(word >> 32);
+    const int bsel = int(g0 & 1u);
+    uint64_t* __restrict__ buf = qb.region + (1 + bsel) * qb.stride;
     if (pos <= qb.cap) {
       // below the capacity: write the keys (a crossing reservation runs into the spare tail)
       int32_t o = pos + incl - cnt;
@@ -521,29 +529,47 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
       __syncwarp();
       if (pos + total <= qb.cap) {
         __threadfence();
-        if (lane == 0) atomicAdd(qb.done, total);
+        if (lane == 0) atomicAdd(qb.done + bsel, total);
         return;
       }
-      // this warp crossed the capacity: once every earlier reservation is written, keep
-      // the k largest keys, publish the k-th as the threshold and reopen the buffer
+      // this warp crossed the capacity of generation g0
       bool ok = true;
-      if (lane == 0) ok = wait_equal(qb.done, pos, qb.wait_limit);
-      ok = __shfl_sync(FULL, int(ok), 0) != 0;
-      if (!ok && lane == 0) atomicOr(qb.fault, 1);
+      if (lane == 0) {
+        // the previous compaction read the other buffer and wrote the keep list
+        ok = wait_equal(qb.cdone, int32_t(g0), qb.wait_limit);
+        // open generation g0 + 1 on the other buffer, empty: the other warps go on there
+        atomicExch(qb.done + (bsel ^ 1), 0);
+        __threadfence();
+        atomicExch(qb.rg, static_cast<unsigned long long>(g0 + 1u) << 32);
+        // every earlier reservation of generation g0 is written
+        ok = wait_equal(qb.done + bsel, pos, qb.wait_limit) && ok;
+        if (!ok) atomicOr(qb.fault, 1);
+      }
+      __syncwarp();
       __threadfence();
-      const uint64_t t = warp_compact(buf, pos + total, qb.k, hist);
+      // the k largest of this buffer and the keep list become the keep list
+      int32_t n = pos + total;
+      uint64_t* __restrict__ keep = qb.region;
+      if (g0 > 0) {
+        for (int32_t j = lane; j < qb.k; j += 32) buf[n + j] = __ldcg(keep + j);
+        n += qb.k;
+        __syncwarp();
+        __threadfence();
+      }
+      const uint64_t t = warp_compact(buf, n, qb.k, hist);
+      for (int32_t j = lane; j < qb.k; j += 32) keep[j] = __ldcg(buf + j);
+      __syncwarp();
       __threadfence();
       if (lane == 0) {
         atomicMax(qb.gthr, (unsigned long long)t);
-        atomicExch(qb.done, qb.k);
         __threadfence();
-        atomicExch(qb.rg, (static_cast<unsigned long long>(g0 + 1u) << 32) | uint32_t(qb.k));
+        atomicExch(qb.cdone, int32_t(g0 + 1u));
       }
       __syncwarp();
       return;
     }
-    // another warp is compacting: wait for the buffer to reopen, then retry against the
-    // raised threshold
+    // generation g0 is full: wait until its crossing warp opens the next one, then retry
+    // against the raised threshold
     bool ok = true;
     if (lane == 0) ok = wait_generation(qb.rg, g0, qb.wait_limit);
     ok = __shfl_sync(FULL, int(ok), 0) != 0;
@@ -553,6 +579,19 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
     }
     thr = max(thr, uint64_t(__ldcg(qb.gthr)));
   }
+}
+
+// Final candidate counts of every query: the keep list (k once a compaction happened) and
+// the open buffer (its written keys); the other buffer was compacted into the keep list.
+__global__ void final_counts_kernel(int32_t B, int32_t k, const unsigned long long* __restrict__ rg,
+                                    const int32_t* __restrict__ done, const int32_t* __restrict__ cdone,
+                                    int32_t* __restrict__ counts) {
+  const int32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= B) return;
+  const int b = int((rg[q] >> 32) & 1ull);
+  counts[3 * q + 0] = cdone[q] > 0 ? k : 0;
+  counts[3 * q + 1] = b == 0 ? done[2 * q] : 0;
+  counts[3 * q + 2] = b == 1 ? done[2 * q + 1] : 0;
 }
 
 // WT: posting weight type; HT: head row type (WT, or float rows for uint8 postings).
@@ -726,8 +765,8 @@ score_kernel(const ScoreParams p) {
         const uint32_t sp = min(span - uint32_t(h * kSel), uint32_t(kSel));
         const uint32_t m = mark_tile(acc + h * kSel, lane, sp, thr);
         if (__any_sync(FULL, m != 0u)) {
-          QueryBuf qb{p.cand + int64_t(q) * p.cand_stride, p.gthr + q, p.rg + q, p.done + q, p.fault,
-                      p.cap, p.k, p.wait_limit};
+          QueryBuf qb{p.cand + int64_t(q) * 3 * p.cand_stride, p.cand_stride, p.gthr + q, p.rg + q,
+                      p.done + 2 * q, p.cdone + q, p.fault, p.cap, p.k, p.wait_limit};
           append_candidates(qb, acc + h * kSel, sp, uint32_t(p.doc_base + d0i + h * kSel), hist, thr, m);
         }
       }
@@ -739,7 +778,8 @@ struct Cfg {
   int npow2 = 0, cap = 0, smem = 0, ctas_per_sm = 0, grid = 0;
   int64_t ecap = 0, n_blocks = 0, n_iblocks = 0, kk = 0, stride = 0;
   int64_t off_nhe = 0, off_hh = 0, off_hw = 0, off_hs = 0, off_nruns = 0, off_rterm = 0, off_rb32 = 0,
-          off_rend = 0, off_rw0 = 0, off_entw = 0, off_cand = 0, off_zero = 0, zero_bytes = 0, total = 0;
+          off_rend = 0, off_rw0 = 0, off_entw = 0, off_cand = 0, off_counts = 0, off_zero = 0, zero_bytes = 0,
+          total = 0;
 };
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
@@ -750,7 +790,7 @@ int64_t align8(int64_t x) { return (x + 7) / 8 * 8; }
 void set_layout(Cfg& c, int64_t B) {
   int64_t o = 0;
   const int64_t E = B * c.ecap;
-  c.stride = c.cap + kSel;
+  c.stride = c.cap + kSel + c.kk;
   c.off_nhe = o; o = align256(o + B * 4);
   c.off_hh = o; o = align256(o + E * 2);
   c.off_hw = o; o = align256(o + E * 4);
@@ -761,10 +801,11 @@ void set_layout(Cfg& c, int64_t B) {
   c.off_rend = o; o = align256(o + E * 2);
   c.off_rw0 = o; o = align256(o + E * 4);
   c.off_entw = o; o = align256(o + E * 4);
-  c.off_cand = o; o = align256(o + B * c.stride * 8);
-  // cleared by every call: thresholds [B] u64, reservation words [B] u64, done [B],
-  // item counter u64, fault flag
-  c.off_zero = o; c.zero_bytes = align8(2 * B * 8 + B * 4) + 16; o = align256(o + c.zero_bytes);
+  c.off_cand = o; o = align256(o + B * 3 * c.stride * 8);
+  c.off_counts = o; o = align256(o + B * 3 * 4);
+  // cleared by every call: thresholds [B] u64, reservation words [B] u64, written
+  // counters [B, 2], finished compactions [B], item counter u64, fault flag
+  c.off_zero = o; c.zero_bytes = align8(2 * B * 8 + 3 * B * 4) + 16; o = align256(o + c.zero_bytes);
   c.total = o;
 }
 
@@ -898,7 +939,9 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.gthr = reinterpret_cast<unsigned long long*>(z);
   p.rg = reinterpret_cast<unsigned long long*>(z + B * 8);
   p.done = reinterpret_cast<int32_t*>(z + 2 * B * 8);
-  p.item_next = reinterpret_cast<unsigned long long*>(z + align8(2 * B * 8 + B * 4));
+  p.cdone = p.done + 2 * B;
+  p.counts = reinterpret_cast<int32_t*>(w + c.off_counts);
+  p.item_next = reinterpret_cast<unsigned long long*>(z + align8(2 * B * 8 + 3 * B * 4));
   p.fault = reinterpret_cast<int32_t*>(p.item_next + 1);
   GSP_CUDA(cudaMemsetAsync(z, 0, size_t(c.zero_bytes), st));
 
@@ -925,8 +968,11 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
     }
     if (rc) return rc;
   }
-  return merge_topk_device(p.cand, B, 1, c.stride, 0, p.done, 1, nullptr, c.kk, out_scores, out_ids,
-                           out_keys, st, -1, p.fault);
+  final_counts_kernel<<<unsigned((B + 255) / 256), 256, 0, st>>>(int32_t(B), int32_t(c.kk), p.rg, p.done,
+                                                                 p.cdone, p.counts);
+  GSP_CHECK_LAUNCH();
+  return merge_topk_device(p.cand, B, 3, 3 * c.stride, c.stride, p.counts, 3, nullptr, c.kk, out_scores,
+                           out_ids, out_keys, st, -1, p.fault);
 }
 
 extern "C" int gsp_set_wait_limit(int32_t polls) {

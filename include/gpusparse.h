@@ -161,9 +161,9 @@ int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const float* qs,
  * or a host that gives the library only its input and output buffers).  No counterpart in
  * the reference.  Scratch is a fixed 32 MiB array compiled into the library, placed on
  * every GPU that loads it and held until exit.  The per-query candidate buffers shrink
- * down to k + 2048 keys (more frequent compactions, same result); a batch that still does
- * not fit (about B * (k + 2048) * 8 bytes plus the plan) is rejected with
- * GSP_ERR_UNSUPPORTED.
+ * to their minimum (more frequent compactions, same result); a batch that still does not
+ * fit (about B * 3 * (2k + 2048) * 8 bytes plus the plan: some 330 queries at k = 1000)
+ * is rejected with GSP_ERR_UNSUPPORTED.
  * Results equal gsp_score_topk's.  The first call on each device looks up the array's
  * device address (cudaGetSymbolAddress) with that device current; make that first call
  * before any stream capture.  All calls on a device share the one array: calls that
