@@ -40,6 +40,9 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 int num_sms();
 int max_smem_optin();
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) only when `bytes` exceeds what was set
+// for this kernel on the current device before.
+int ensure_smem(const void* func, int bytes);
 
 // Exact top-k over packed candidate lists (select.cu); counts either on the device
 // (counts_dev[b * cstride_b + r]) or, for at most 64 lists, on the host.

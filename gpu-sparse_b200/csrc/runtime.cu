@@ -1,6 +1,10 @@
 // Error reporting, device queries and a device-wide exclusive scan (int32 -> int64).
 #include "common.cuh"
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include <string.h>
 
 namespace gsp {
@@ -19,6 +23,23 @@ int num_sms() {
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
   return n;
+}
+
+// Raises a kernel's dynamic shared-memory limit only when a launch needs more than was set
+// before on this device, so repeated calls (and calls inside a stream capture, after a
+// first call outside it) make no attribute call.
+int ensure_smem(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> done;
+  int dev = 0;
+  GSP_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> g(mu);
+  int& cur = done[{dev, func}];
+  if (bytes > cur) {
+    GSP_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    cur = bytes;
+  }
+  return GSP_OK;
 }
 
 int max_smem_optin() {

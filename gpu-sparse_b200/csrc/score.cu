@@ -859,7 +859,7 @@ Profile& profile() {
 template <typename WT, typename HT>
 int launch_score(const ScoreParams& p, const Cfg& c, cudaStream_t st) {
   auto kern = score_kernel<WT, HT>;
-  GSP_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem));
+  if (int rc = ensure_smem(reinterpret_cast<const void*>(kern), c.smem)) return rc;
   Profile& pr = profile();
   std::pair<cudaEvent_t, cudaEvent_t>* evp = nullptr;
   {
@@ -948,7 +948,8 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   GSP_CUDA(cudaMemsetAsync(z, 0, size_t(c.zero_bytes), st));
 
   const size_t plan_smem = size_t(c.npow2) * 8;
-  GSP_CUDA(cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(plan_smem)));
+  rc = ensure_smem(reinterpret_cast<const void*>(plan_kernel), int(plan_smem));
+  if (rc) return rc;
   plan_kernel<<<unsigned(B), kPlanThreads, plan_smem, st>>>(
       qi, qs, int32_t(B), int32_t(W), ix->V, c.npow2, ix->offsets, ix->head_slot, ix->n_head,
       ix->wdtype == GSP_W_U8 ? ix->term_scale : nullptr, p);

@@ -243,7 +243,7 @@ int merge_topk_device(const uint64_t* keys, int64_t B, int64_t R, int64_t stride
   int32_t kpow2 = 1;
   while (kpow2 < k) kpow2 <<= 1;
   const size_t smem = size_t(kpow2) * 8;
-  GSP_CUDA(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  if (int rc = ensure_smem(reinterpret_cast<const void*>(merge_kernel), int(smem))) return rc;
   merge_kernel<<<unsigned(B), kMergeThreads, smem, st>>>(keys, stride_b, stride_r, int32_t(R), fault,
                                                          counts_dev, cstride_b, cp, use_param, int32_t(k),
                                                          int32_t(k), kpow2, pad_id, out_scores, out_ids,

@@ -11,7 +11,7 @@ from .index import (BLOCK_DOCS, BLOCK_SIZE, VOCAB_SIZE, GPUInvertedIndex,  # noq
                     build_gpu_inverted_index_from_sparse, build_index_from_scipy,
                     dequantized_weights, generate_synthetic_splade_data, index_memory_stats,
                     load_index, quantize_, save_index)
-from .scoring import (build_chunk_boundaries, compacted_topk, merge_topk,  # noqa: F401
+from .scoring import (CapturedScorer, build_chunk_boundaries, compacted_topk, merge_topk,  # noqa: F401
                       score_topk, triton_chunked_score, triton_chunked_score_fused,
                       triton_fused_score, triton_wand_score)
 

@@ -156,13 +156,15 @@ def dequantized_weights(index: GPUInvertedIndex) -> torch.Tensor:
 
 
 def ensure_blocks(index: GPUInvertedIndex) -> None:
-    """Derive block_starts for an index constructed without them (e.g. field by field, as
-    the reference's plug-in does); validates that lists strictly ascend (ValueError for a
+    """Derive the scorer's block rows (1024-document blocks) for an index constructed
+    without them (e.g. field by field, as the reference's plug-in does) or built with
+    another block size; validates that lists strictly ascend (ValueError for a
     descending step or a repeated doc id)."""
-    if getattr(index, "block_starts", None) is not None:
+    if getattr(index, "block_starts", None) is not None and \
+            (getattr(index, "block_docs", None) or BLOCK_DOCS) == BLOCK_DOCS:
         return
     from .scoring import build_chunk_boundaries
-    bd = getattr(index, "block_docs", None) or BLOCK_DOCS
+    bd = BLOCK_DOCS
     dev = index.device if isinstance(index.device, torch.device) else torch.device(index.device)
     n_bad, n_dup = ctypes.c_int64(0), ctypes.c_int64(0)
     with torch.cuda.device(dev):

@@ -192,3 +192,60 @@ def merge_topk(keys: torch.Tensor, counts, k: int, stride_r: Optional[int] = Non
         L.check(L.lib().gsp_merge_topk(L.ptr(keys), B, R, kin, B * kin, cnt, k, L.ptr(s),
                                        L.ptr(i), None, L.stream_of(dev)), "merge_topk")
     return s, i
+
+
+class CapturedScorer:
+    """Exact top-k of fixed-shape query batches replayed from one CUDA graph (no reference
+    counterpart).  The query, output and workspace buffers are allocated once, one call of
+    the fused path (query plan, scorer, merge) is captured after a first call outside the
+    capture, and every ``run`` copies a batch in and replays the graph on the current
+    stream; the launch cost is then paid once per batch instead of once per kernel.  Meant
+    for serving loops with small batches.
+
+    ``run`` returns the scorer's own output tensors, which the next ``run`` overwrites.
+    """
+
+    def __init__(self, index: GPUInvertedIndex, batch: int, width: int, top_k: int = 10):
+        if batch < 1 or width < 1 or top_k < 1:
+            raise ValueError("batch, width and top_k must be positive")
+        self.index = index
+        self.B, self.W = int(batch), int(width)
+        self.k = min(int(top_k), int(index.num_docs))
+        dev = index.device
+        self.qi = torch.full((self.B, self.W), -1, dtype=torch.int32, device=dev)
+        self.qs = torch.zeros((self.B, self.W), dtype=torch.float32, device=dev)
+        self.s = torch.empty((self.B, self.k), dtype=torch.float32, device=dev)
+        self.i = torch.empty((self.B, self.k), dtype=torch.int64, device=dev)
+        lib = L.lib()
+        with torch.cuda.device(dev):
+            self._v = view(index)                     # block and head rows exist from here on
+            nbytes = lib.gsp_score_ws_bytes(ctypes.byref(self._v), self.B, self.W, self.k)
+            if nbytes < 0:
+                L.check(int(-nbytes), "CapturedScorer")
+            self.ws = L.workspace(nbytes, dev)
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                self._launch()                        # first call: attributes, symbol set-up
+            torch.cuda.current_stream(dev).wait_stream(side)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=side):
+                self._launch()
+
+    def _launch(self) -> None:
+        dev = self.index.device
+        L.check(L.lib().gsp_score_topk(ctypes.byref(self._v), L.ptr(self.qi), L.ptr(self.qs), self.B,
+                                       self.W, self.k, L.ptr(self.s), L.ptr(self.i), None,
+                                       L.ptr(self.ws), self.ws.numel(), L.stream_of(dev)),
+                "CapturedScorer")
+
+    def run(self, query_term_ids: torch.Tensor, query_term_scores: torch.Tensor):
+        """Scores one batch of exactly (batch, width) queries; returns (scores, ids)."""
+        qi, qs = _prep_queries(self.index, query_term_ids, query_term_scores)
+        if tuple(qi.shape) != (self.B, self.W):
+            raise ValueError(f"batch must be {(self.B, self.W)}, got {tuple(qi.shape)}")
+        with torch.cuda.device(self.index.device):
+            self.qi.copy_(qi)
+            self.qs.copy_(qs)
+            self.graph.replay()
+        return self.s, self.i

@@ -183,3 +183,35 @@ def test_index_save_load_round_trip(tmp_path, wd):
     torch.save({"x": 1}, tmp_path / "other.pt")
     with pytest.raises(ValueError):
         gpusparse.load_index(tmp_path / "other.pt", DEV)
+
+
+def test_index_built_with_other_block_size_scores():
+    import gpusparse
+    ip, ix, dt = O.synth_csr(9000, 30522, seed=32)
+    g = gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), 30522, DEV, block_docs=4096)
+    qi, qs = O.synth_queries(16, 30522, seed=33)
+    s, i = gpusparse.triton_fused_score(g, t(qi), t(qs), top_k=300)
+    assert g.block_docs == 1024
+    rs, ri = O.score_topk(O.build_index(ip, ix, dt, 30522), qi, qs, 300, head=g.head_ids.cpu().numpy())
+    assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
+
+
+def test_captured_scorer_replays_equal_eager_calls():
+    import gpusparse
+    ip, ix, dt = O.synth_csr(20000, 30522, seed=34)
+    g = gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), 30522, DEV)
+    qi0, _ = O.synth_queries(32, 30522, seed=35)
+    cap = gpusparse.CapturedScorer(g, 32, qi0.shape[1] + 8, top_k=500)
+    for seed in (35, 36, 37):
+        qi, qs = O.synth_queries(32, 30522, seed=seed)
+        W = cap.W
+        pi = np.full((32, W), -1, dtype=np.int32)
+        ps = np.zeros((32, W), dtype=np.float32)
+        w = min(W, qi.shape[1])
+        pi[:, :w], ps[:, :w] = qi[:, :w], qs[:, :w]
+        s, i = cap.run(t(pi), t(ps))
+        es, ei = gpusparse.triton_fused_score(g, t(pi), t(ps), top_k=500)
+        torch.cuda.synchronize()
+        assert torch.equal(i, ei) and torch.equal(s.view(torch.int32), es.view(torch.int32))
+    with pytest.raises(ValueError):
+        cap.run(t(pi[:5]), t(ps[:5]))
