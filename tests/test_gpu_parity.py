@@ -200,3 +200,22 @@ def test_shards_merge_equals_unsharded(corpus):
         s, i = gpusparse.merge_topk(allk, ShardLayout(N, world, 0).list_counts(k), k)
         rs, ri = O.score_topk(oidx, qi, qs, k, head=head)
         assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
+
+
+def test_supported_limits_max_k_and_max_width(corpus, gindex):
+    """top_k = 8192 and W = 4096 (the supported maxima) stay exact; W = 4097 is refused."""
+    import gpusparse
+    _, _, _, oidx = corpus
+    qi, qs = O.synth_queries(8, V, seed=50)
+    s, i = gpusparse.triton_fused_score(gindex, t(qi), t(qs), top_k=8192)
+    rs, ri = O.score_topk(oidx, qi, qs, 8192, head=hd(gindex))
+    assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
+    rng = np.random.default_rng(51)
+    wi = rng.integers(0, V, size=(4, 4096)).astype(np.int32)
+    ws = rng.random((4, 4096)).astype(np.float32)
+    s, i = gpusparse.triton_fused_score(gindex, t(wi), t(ws), top_k=100)
+    rs, ri = O.score_topk(oidx, wi, ws, 100, head=hd(gindex))
+    assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
+    with pytest.raises(RuntimeError):
+        gpusparse.triton_fused_score(gindex, t(np.zeros((2, 4097), np.int32)),
+                                     t(np.zeros((2, 4097), np.float32)), top_k=10)
