@@ -614,8 +614,10 @@ score_kernel(const ScoreParams p) {
     if (it >= n_items) break;
     // claim the next item now, so the atomic's round trip overlaps this item's work
     if (lane == 0) nit = atomicAdd(p.item_next, 1ull);
-    const int32_t b = int32_t(it / unsigned(p.B));
-    const int32_t q = int32_t(it - (unsigned long long)b * unsigned(p.B));
+    // items stay below 2^31 (make_cfg), so 32-bit division suffices
+    const uint32_t it32 = uint32_t(it);
+    const int32_t b = int32_t(it32 / uint32_t(p.B));
+    const int32_t q = int32_t(it32 - uint32_t(b) * uint32_t(p.B));
     const int64_t pbase = int64_t(q) * p.ecap;
     const int32_t nhe = p.n_head_e[q];
     const int32_t nr = p.n_runs[q];
