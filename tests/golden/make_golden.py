@@ -41,7 +41,7 @@ import torch  # noqa: E402
 
 from oracle import oracle as O  # noqa: E402
 
-REF = os.environ.get("GPUSPARSE_REF", "/root/reference")
+REF = os.environ.get("GPUSPARSE_REF", "")
 
 
 def sha(*arrs) -> str:
@@ -53,6 +53,8 @@ def sha(*arrs) -> str:
 
 
 def import_reference():
+    if not REF or not os.path.isdir(os.path.join(REF, "src")):
+        raise SystemExit("set GPUSPARSE_REF to the reference checkout (the directory holding src/)")
     sys.path.insert(0, os.path.join(REF, "src"))
     sys.path.insert(0, REF)
     import triton_kernel, triton_kernel_chunked, fused_topk  # noqa: E401
