@@ -6,9 +6,9 @@
 // Work decomposition.  A work item is one (document tile, query) pair.  Warps take items
 // from one global counter in tile-major order, so the whole GPU works on a window of a few
 // tiles at any moment (their postings and dense head rows stay in L2) and no warp idles
-// while items are left.  The tile is one index block (1024 documents), so the window of
-// every term's postings inside a tile is [block_starts[b][t], block_starts[b+1][t]) with
-// no search.  The warp owns the tile's fp32 accumulators, so every (query, document) cell
+// while items are left.  A tile is a whole number of index blocks (one, 1024 documents,
+// by default), so the window of every term's postings inside a tile is
+// [block_starts[first block][t], block_starts[last block + 1][t]) with no search.  The warp owns the tile's fp32 accumulators, so every (query, document) cell
 // has exactly one writer, and the result does not depend on which warp scored which item.
 //
 // Candidates.  Each query has two candidate buffers used in turn and a keep list of the k
@@ -29,8 +29,9 @@
 //
 // Per tile:
 //  1. head terms (the index's densest terms, stored as dense rows): the warp keeps the
-//     1024 accumulators in registers (32 per lane) and streams each head row of the query
-//     with coalesced vector loads: acc = fma(q_w, w, acc) for every document;
+//     accumulators of one part of the tile in registers (512 documents, 16 per lane, with
+//     four CTAs per SM) and streams the matching slice of each of the query's head rows
+//     with coalesced 16-byte loads: acc = fma(q_w, w, acc) for every document;
 //  2. the accumulators go to shared memory and the tail terms (all others), in ascending
 //     term id, are scattered into them: a run whose window is long (or that a query
 //     repeats) is streamed on its own, four 32-posting chunks in flight; consecutive short
