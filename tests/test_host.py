@@ -117,3 +117,42 @@ def test_oracle_quantisation_roundtrip():
     err = np.abs(w[real] - idx.scores[real])
     term_of = np.repeat(np.arange(30522), idx.padded_lengths)[real]
     assert np.all(err <= scale[term_of] * 0.5 + 1e-7)
+
+
+def test_plugin_retrieve_pipeline_with_a_stand_in_scorer(monkeypatch):
+    """The plug-in's batch pipeline (score batch i+1 while batch i is formatted) on the CPU
+    with a stand-in scorer: batches are collected in order, rows keep the scorer's order,
+    scores <= 0 are dropped and doc ids are mapped to the caller's names."""
+    import torch
+    from lsr_benchmark_engine import gpusparse_retrieval as P
+
+    class Idx:
+        num_docs = 50
+
+    def fake_score(index, qi, qs, top_k=10, block_pl=128):
+        B = qi.shape[0]
+        base = qi[:, 0].to(torch.float32)                 # row identity from the query
+        s = base[:, None] - torch.arange(top_k, dtype=torch.float32)[None, :]
+        ids = (qi[:, :1].long() + torch.arange(top_k)[None, :]) % Idx.num_docs
+        return s, ids
+
+    class Ev:
+        def record(self, stream=None):
+            pass
+
+        def synchronize(self):
+            pass
+
+    monkeypatch.setattr(P, "triton_fused_score", fake_score)
+    monkeypatch.setattr(P.torch.cuda, "Event", lambda *a, **k: Ev())
+    monkeypatch.setattr(P.torch.cuda, "current_stream", lambda *a, **k: None)
+    monkeypatch.setattr(P.torch.cuda, "is_available", lambda: False)
+    n = 23
+    qi = torch.arange(n, dtype=torch.int32)[:, None].repeat(1, 3)
+    qs = torch.ones((n, 3))
+    names = [f"doc{d}" for d in range(Idx.num_docs)]
+    res = P.retrieve(Idx(), [f"q{j}" for j in range(n)], qi, qs, names, k=5, batch_size=4)
+    assert len(res) == n
+    for j, row in enumerate(res):
+        exp = [(f"q{j}", float(j - r), f"doc{(j + r) % 50}") for r in range(5) if j - r > 0]
+        assert row == exp
