@@ -156,3 +156,27 @@ def test_plugin_retrieve_pipeline_with_a_stand_in_scorer(monkeypatch):
     for j, row in enumerate(res):
         exp = [(f"q{j}", float(j - r), f"doc{(j + r) % 50}") for r in range(5) if j - r > 0]
         assert row == exp
+
+
+def test_index_view_layout_matches_the_header(tmp_path):
+    """gsp_index_view as the C compiler lays it out (sizeof, offsetof) equals the ctypes
+    binding's layout, so a caller of the C ABI and the Python wrapper agree."""
+    import ctypes
+    import shutil
+    import subprocess
+    import gpusparse._lib as L
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    inc = os.path.join(ROOT, "include")
+    names = [f[0] for f in L.IndexView._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "gpusparse.h"\nint main(void) {\n'
+                   '  printf("size %zu\\n", sizeof(gsp_index_view));\n'
+                   + "".join(f'  printf("{n} %zu\\n", offsetof(gsp_index_view, {n}));\n' for n in names)
+                   + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.check_call(["gcc", "-I", inc, str(src), "-o", str(exe)])
+    got = dict(line.split() for line in subprocess.check_output([str(exe)], text=True).splitlines())
+    assert int(got["size"]) == ctypes.sizeof(L.IndexView)
+    for n in names:
+        assert int(got[n]) == getattr(L.IndexView, n).offset, n
