@@ -13,6 +13,10 @@
 //   fill  : one warp per block walks its documents in order and appends each posting at
 //           offsets[t] + block_starts[b][t] + (running count of t in b); documents are
 //           visited in ascending order, so every list comes out sorted by doc id.
+//
+// Both passes work on any run of whole blocks, so a corpus can also be built in chunks of
+// documents (count every chunk, finish the counts, fill every chunk, finish the fill):
+// only one chunk of the CSR needs to be on the device at a time.
 #include "common.cuh"
 
 namespace gsp {
@@ -21,14 +25,14 @@ namespace {
 constexpr int kCountThreads = 512;
 
 __global__ void __launch_bounds__(kCountThreads)
-count_kernel(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* __restrict__ indptr,
-             const int32_t* __restrict__ indices, uint32_t* __restrict__ counts,
-             int32_t use_smem, int32_t* __restrict__ err) {
+count_kernel(int64_t n_docs, int32_t V, int32_t block_docs, int64_t first_block,
+             const int64_t* __restrict__ indptr, const int32_t* __restrict__ indices,
+             uint32_t* __restrict__ counts, int32_t use_smem, int32_t* __restrict__ err) {
   extern __shared__ uint32_t hist[];
-  const int64_t b = blockIdx.x;
+  const int64_t b = blockIdx.x;               // block of this chunk (documents local to it)
   const int64_t d0 = b * block_docs;
   const int64_t d1 = min(d0 + block_docs, n_docs);
-  uint32_t* row = counts + b * int64_t(V);
+  uint32_t* row = counts + (first_block + b) * int64_t(V);
   if (use_smem) {
     for (int32_t t = threadIdx.x; t < V; t += blockDim.x) hist[t] = 0u;
     __syncthreads();
@@ -49,16 +53,17 @@ count_kernel(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* __res
   }
 }
 
-// per term: exclusive prefix over blocks (in place), lengths, padded lengths
-__global__ void scan_blocks_kernel(int32_t V, int64_t n_blocks, uint32_t* __restrict__ counts,
-                                   uint32_t* __restrict__ block_starts, int32_t* __restrict__ lengths,
-                                   int32_t* __restrict__ padded, int32_t* __restrict__ err) {
+// per term: exclusive prefix over blocks, in place (rows 0..n_blocks-1 hold the counts on
+// entry; row n_blocks receives the totals), lengths, padded lengths
+__global__ void scan_blocks_kernel(int32_t V, int64_t n_blocks, uint32_t* __restrict__ block_starts,
+                                   int32_t* __restrict__ lengths, int32_t* __restrict__ padded,
+                                   int32_t* __restrict__ err) {
   const int32_t t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= V) return;
   uint64_t run = 0;
   uint32_t max_c = 0;
   for (int64_t b = 0; b < n_blocks; ++b) {
-    const uint32_t c = counts[b * V + t];
+    const uint32_t c = block_starts[b * V + t];
     max_c = max(max_c, c);
     block_starts[b * V + t] = uint32_t(run);
     run += c;
@@ -69,18 +74,22 @@ __global__ void scan_blocks_kernel(int32_t V, int64_t n_blocks, uint32_t* __rest
   padded[t] = int32_t((run + kPostingPad - 1) / kPostingPad * kPostingPad);
 }
 
-// One warp per document block; u16 running counts per term in shared memory.
+// One warp per document block; u16 running counts per term in shared memory.  A posting
+// is written only inside its block's slice of the term's list, [block_starts[b][t],
+// block_starts[b+1][t]); rows that hold more postings of a term than the count pass saw
+// (a chunk filled with other rows than it was counted with) set err = 3 and are dropped.
 __global__ void __launch_bounds__(32)
-fill_kernel(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* __restrict__ indptr,
-            const int32_t* __restrict__ indices, const float* __restrict__ data,
-            const int64_t* __restrict__ offsets, const uint32_t* __restrict__ block_starts,
-            int32_t* __restrict__ doc_ids, float* __restrict__ weights) {
+fill_kernel(int64_t n_docs, int32_t V, int32_t block_docs, int64_t first_doc,
+            const int64_t* __restrict__ indptr, const int32_t* __restrict__ indices,
+            const float* __restrict__ data, const int64_t* __restrict__ offsets,
+            const uint32_t* __restrict__ block_starts, int32_t* __restrict__ doc_ids,
+            float* __restrict__ weights, int32_t* __restrict__ err) {
   extern __shared__ uint16_t run16[];
   const int lane = lane_id();
-  const int64_t b = blockIdx.x;
+  const int64_t b = blockIdx.x;               // block of this chunk (documents local to it)
   const int64_t d0 = b * block_docs;
   const int64_t d1 = min(d0 + block_docs, n_docs);
-  const uint32_t* bstart = block_starts + b * int64_t(V);
+  const uint32_t* bstart = block_starts + (first_doc / block_docs + b) * int64_t(V);
   for (int32_t t = lane; t < V; t += 32) run16[t] = 0;
   __syncwarp();
   for (int64_t d = d0; d < d1; ++d) {
@@ -102,29 +111,54 @@ fill_kernel(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* __rest
       }
       old = __shfl_sync(FULL, old, leader);
       if (live) {
-        const int64_t pos = offsets[t] + int64_t(__ldg(bstart + t)) + old + rank;
-        doc_ids[pos] = int32_t(d);
-        weights[pos] = w;
+        const uint32_t s0 = __ldg(bstart + t), s1 = __ldg(bstart + V + t);
+        if (old + rank < s1 - s0) {
+          const int64_t pos = offsets[t] + int64_t(s0) + old + rank;
+          doc_ids[pos] = int32_t(first_doc + d);
+          weights[pos] = w;
+        } else {
+          atomicExch(err, 3);
+        }
       }
       __syncwarp();
     }
   }
 }
 
-// max weight per term (0 for an empty list), one warp per term
-__global__ void max_kernel(int32_t V, const int64_t* __restrict__ offsets,
-                           const int32_t* __restrict__ lengths, const float* __restrict__ weights,
-                           float* __restrict__ max_scores) {
+// One warp per term, after every posting is in place: writes the list's padding (doc id -1,
+// weight 0), its max weight (0 for an empty list), and counts lists that are out of order
+// or hold a doc id outside [0, n_docs) (n_bad[0]) and lists that repeat a doc id (n_bad[1]).
+__global__ void finish_kernel(int64_t n_docs, int32_t V, const int64_t* __restrict__ offsets,
+                              const int32_t* __restrict__ lengths, int32_t* __restrict__ doc_ids,
+                              float* __restrict__ weights, float* __restrict__ max_scores,
+                              unsigned long long* __restrict__ n_bad) {
   const int32_t t = (int32_t)((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
   const int lane = lane_id();
   if (t >= V) return;
   const int64_t o = offsets[t];
   const int32_t L = lengths[t];
+  const int32_t P = (L + kPostingPad - 1) / kPostingPad * kPostingPad;
   float m = -INFINITY;
-  for (int32_t p = lane; p < L; p += 32) m = fmaxf(m, weights[o + p]);
+  bool bad = false, dup = false;
+  for (int32_t p = lane; p < L; p += 32) {
+    m = fmaxf(m, weights[o + p]);
+    const int32_t b = doc_ids[o + p];
+    bad |= b < 0 || int64_t(b) >= n_docs;
+    if (p > 0) {
+      const int32_t a = doc_ids[o + p - 1];
+      bad |= b < a;
+      dup |= b == a;
+    }
+  }
+  for (int32_t p = L + lane; p < P; p += 32) {
+    doc_ids[o + p] = -1;
+    weights[o + p] = 0.0f;
+  }
 #pragma unroll
   for (int s = 16; s; s >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, s));
   if (lane == 0) max_scores[t] = L > 0 ? m : 0.0f;
+  if (__any_sync(FULL, bad) && lane == 0) atomicAdd(n_bad, 1ull);
+  if (__any_sync(FULL, dup) && lane == 0) atomicAdd(n_bad + 1, 1ull);
 }
 
 __global__ void quant_kernel(int32_t V, const int64_t* __restrict__ offsets,
@@ -225,13 +259,14 @@ int64_t n_blocks_of(int64_t n_docs, int32_t block_docs) {
 
 using namespace gsp;
 
-// workspace: counts [n_blocks * V] u32 | err int32 | scan ws
+// workspace: err int32 at 0 | finish counters (2 x u64) at 64 | scan ws at 256.  The block
+// counts are accumulated in block_starts itself and scanned in place.
+constexpr int64_t kWsCounters = 64;
+constexpr int64_t kWsScan = 256;
+
 extern "C" int64_t gsp_index_ws_bytes(int64_t n_docs, int32_t V, int32_t block_docs) {
   if (n_docs < 0 || V <= 0 || block_docs <= 0) return -1;
-  const int64_t nb = n_blocks_of(n_docs, block_docs);
-  int64_t bytes = ((nb * V * 4 + 255) / 256) * 256 + 256;
-  bytes += gsp_scan_ws_bytes(V);
-  return bytes;
+  return kWsScan + gsp_scan_ws_bytes(V);
 }
 
 static int check_csr_args(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* indptr) {
@@ -242,41 +277,67 @@ static int check_csr_args(int64_t n_docs, int32_t V, int32_t block_docs, const i
   return GSP_OK;
 }
 
-extern "C" int gsp_index_count(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* indptr,
-                               const int32_t* indices, int32_t* lengths, int32_t* padded,
-                               int64_t* offsets, uint32_t* block_starts, int64_t* total_padded,
-                               void* ws, int64_t ws_bytes, void* stream) {
+static int check_chunk_args(int64_t n_docs, int32_t V, int32_t block_docs, int64_t first_doc,
+                            int64_t chunk_docs, const int64_t* indptr, void* ws, int64_t ws_bytes) {
   int rc = check_csr_args(n_docs, V, block_docs, indptr);
   if (rc) return rc;
-  GSP_REQUIRE(ws_bytes >= gsp_index_ws_bytes(n_docs, V, block_docs), GSP_ERR_ARG,
-              "gsp_index_count: workspace too small");
+  GSP_REQUIRE(ws && ws_bytes >= gsp_index_ws_bytes(n_docs, V, block_docs), GSP_ERR_ARG,
+              "index build: workspace too small");
+  GSP_REQUIRE(first_doc >= 0 && chunk_docs >= 0 && first_doc + chunk_docs <= n_docs &&
+                  first_doc % block_docs == 0 &&
+                  (chunk_docs % block_docs == 0 || first_doc + chunk_docs == n_docs),
+              GSP_ERR_ARG,
+              "index build: chunk [%lld, %lld) of %lld documents is not a run of whole %d-document "
+              "blocks",
+              (long long)first_doc, (long long)(first_doc + chunk_docs), (long long)n_docs, block_docs);
+  return GSP_OK;
+}
+
+extern "C" int gsp_index_count_chunk(int64_t n_docs, int32_t V, int32_t block_docs, int64_t first_doc,
+                                     int64_t chunk_docs, const int64_t* indptr, const int32_t* indices,
+                                     uint32_t* block_starts, void* ws, int64_t ws_bytes, void* stream) {
+  int rc = check_chunk_args(n_docs, V, block_docs, first_doc, chunk_docs, indptr, ws, ws_bytes);
+  if (rc) return rc;
+  GSP_REQUIRE(block_starts, GSP_ERR_ARG, "gsp_index_count_chunk: block_starts is null");
+  cudaStream_t st = as_stream(stream);
+  int32_t* err = static_cast<int32_t*>(ws);
+  if (first_doc == 0) GSP_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), st));
+  const int64_t nb = n_blocks_of(chunk_docs, block_docs);
+  if (nb == 0) return GSP_OK;
+  uint32_t* rows = block_starts + (first_doc / block_docs) * int64_t(V);
+  const size_t smem = size_t(V) * 4;
+  const int use_smem = smem <= size_t(max_smem_optin()) ? 1 : 0;
+  if (use_smem) {
+    rc = ensure_smem(reinterpret_cast<const void*>(count_kernel), int(smem));
+    if (rc) return rc;
+  } else {
+    GSP_CUDA(cudaMemsetAsync(rows, 0, size_t(nb) * V * 4, st));
+  }
+  count_kernel<<<unsigned(nb), kCountThreads, use_smem ? smem : 0, st>>>(
+      chunk_docs, V, block_docs, 0, indptr, indices, rows, use_smem, err);
+  GSP_CHECK_LAUNCH();
+  return GSP_OK;
+}
+
+extern "C" int gsp_index_count_finish(int64_t n_docs, int32_t V, int32_t block_docs, int32_t* lengths,
+                                      int32_t* padded, int64_t* offsets, uint32_t* block_starts,
+                                      int64_t* total_padded, void* ws, int64_t ws_bytes, void* stream) {
+  int64_t dummy_indptr = 0;
+  int rc = check_chunk_args(n_docs, V, block_docs, 0, 0, &dummy_indptr, ws, ws_bytes);
+  if (rc) return rc;
+  GSP_REQUIRE(lengths && padded && offsets && block_starts && total_padded, GSP_ERR_ARG,
+              "gsp_index_count_finish: bad arguments");
   cudaStream_t st = as_stream(stream);
   const int64_t nb = n_blocks_of(n_docs, block_docs);
   char* w = static_cast<char*>(ws);
-  uint32_t* counts = reinterpret_cast<uint32_t*>(w);
-  int32_t* err = reinterpret_cast<int32_t*>(w + ((nb * V * 4 + 255) / 256) * 256);
-  void* scan_ws = w + ((nb * V * 4 + 255) / 256) * 256 + 256;
-  GSP_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), st));
-  if (nb > 0) {
-    const size_t smem = size_t(V) * 4;
-    const int use_smem = smem <= size_t(max_smem_optin()) ? 1 : 0;
-    if (use_smem) {
-      GSP_CUDA(cudaFuncSetAttribute(count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    int(smem)));
-    } else {
-      GSP_CUDA(cudaMemsetAsync(counts, 0, size_t(nb) * V * 4, st));
-    }
-    count_kernel<<<unsigned(nb), kCountThreads, use_smem ? smem : 0, st>>>(
-        n_docs, V, block_docs, indptr, indices, counts, use_smem, err);
-    GSP_CHECK_LAUNCH();
-  }
-  scan_blocks_kernel<<<unsigned((V + 255) / 256), 256, 0, st>>>(V, nb, counts, block_starts, lengths,
-                                                                padded, err);
+  int32_t* err = reinterpret_cast<int32_t*>(w);
+  if (n_docs == 0) GSP_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), st));
+  scan_blocks_kernel<<<unsigned((V + 255) / 256), 256, 0, st>>>(V, nb, block_starts, lengths, padded,
+                                                                err);
   GSP_CHECK_LAUNCH();
-  rc = gsp_scan_i32(padded, V, offsets, scan_ws, gsp_scan_ws_bytes(V), stream);
+  rc = gsp_scan_i32(padded, V, offsets, w + kWsScan, gsp_scan_ws_bytes(V), stream);
   if (rc) return rc;
-  // offsets has V+1 slots' worth only when the caller passes V+1; read the total from the
-  // last offset plus the last padded length instead
+  // offsets holds V entries; the total is the last offset plus the last padded length
   int64_t last_off = 0;
   int32_t last_pad = 0, herr = 0;
   GSP_CUDA(cudaMemcpyAsync(&last_off, offsets + (V - 1), sizeof(int64_t), cudaMemcpyDeviceToHost, st));
@@ -291,46 +352,84 @@ extern "C" int gsp_index_count(int64_t n_docs, int32_t V, int32_t block_docs, co
   return GSP_OK;
 }
 
+extern "C" int gsp_index_fill_chunk(int64_t n_docs, int32_t V, int32_t block_docs, int64_t first_doc,
+                                    int64_t chunk_docs, const int64_t* indptr, const int32_t* indices,
+                                    const float* data, const int64_t* offsets,
+                                    const uint32_t* block_starts, int32_t* doc_ids, float* weights,
+                                    void* ws, int64_t ws_bytes, void* stream) {
+  int rc = check_chunk_args(n_docs, V, block_docs, first_doc, chunk_docs, indptr, ws, ws_bytes);
+  if (rc) return rc;
+  GSP_REQUIRE(offsets && block_starts && (chunk_docs == 0 || (indices && data && doc_ids && weights)),
+              GSP_ERR_ARG, "gsp_index_fill_chunk: bad arguments");
+  const int64_t nb = n_blocks_of(chunk_docs, block_docs);
+  if (nb == 0) return GSP_OK;
+  const size_t smem = size_t(V) * 2;
+  GSP_REQUIRE(smem <= size_t(max_smem_optin()), GSP_ERR_UNSUPPORTED,
+              "index build: vocabulary %d too large", V);
+  rc = ensure_smem(reinterpret_cast<const void*>(fill_kernel), int(smem));
+  if (rc) return rc;
+  fill_kernel<<<unsigned(nb), 32, smem, as_stream(stream)>>>(chunk_docs, V, block_docs, first_doc,
+                                                             indptr, indices, data, offsets,
+                                                             block_starts, doc_ids, weights,
+                                                             static_cast<int32_t*>(ws));
+  GSP_CHECK_LAUNCH();
+  return GSP_OK;
+}
+
+extern "C" int gsp_index_fill_finish(int64_t n_docs, int32_t V, const int64_t* offsets,
+                                     const int32_t* lengths, int32_t* doc_ids, float* weights,
+                                     float* max_scores, void* ws, int64_t ws_bytes, void* stream) {
+  GSP_REQUIRE(n_docs >= 0 && V > 0 && offsets && lengths && max_scores && ws &&
+                  ws_bytes >= kWsCounters + 16,
+              GSP_ERR_ARG, "gsp_index_fill_finish: bad arguments");
+  cudaStream_t st = as_stream(stream);
+  unsigned long long* d_cnt =
+      reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + kWsCounters);
+  GSP_CUDA(cudaMemsetAsync(d_cnt, 0, 16, st));
+  int32_t herr = 0;
+  GSP_CUDA(cudaMemcpyAsync(&herr, ws, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  finish_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, st>>>(
+      n_docs, V, offsets, lengths, doc_ids, weights, max_scores, d_cnt);
+  GSP_CHECK_LAUNCH();
+  unsigned long long h[2] = {0, 0};
+  GSP_CUDA(cudaMemcpyAsync(h, d_cnt, 16, cudaMemcpyDeviceToHost, st));
+  GSP_CUDA(cudaStreamSynchronize(st));
+  GSP_REQUIRE(herr != 3, GSP_ERR_ARG,
+              "index build: a chunk was filled with other rows than it was counted with");
+  GSP_REQUIRE(h[0] == 0, GSP_ERR_ARG,
+              "index build: %llu posting lists are out of place; every chunk must be counted and "
+              "filled exactly once with the same CSR rows",
+              h[0]);
+  // a term listed twice in one document row would give one list a repeated doc id; the
+  // scorer applies a list's postings to distinct documents in parallel, so that is refused
+  GSP_REQUIRE(h[1] == 0, GSP_ERR_UNSORTED,
+              "index build: %llu terms occur twice in one document row (duplicate (doc, term) "
+              "entries); merge them first, e.g. scipy's csr_matrix.sum_duplicates()", h[1]);
+  return GSP_OK;
+}
+
+extern "C" int gsp_index_count(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* indptr,
+                               const int32_t* indices, int32_t* lengths, int32_t* padded,
+                               int64_t* offsets, uint32_t* block_starts, int64_t* total_padded,
+                               void* ws, int64_t ws_bytes, void* stream) {
+  int rc = gsp_index_count_chunk(n_docs, V, block_docs, 0, n_docs, indptr, indices, block_starts, ws,
+                                 ws_bytes, stream);
+  if (rc) return rc;
+  return gsp_index_count_finish(n_docs, V, block_docs, lengths, padded, offsets, block_starts,
+                                total_padded, ws, ws_bytes, stream);
+}
+
 extern "C" int gsp_index_fill(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* indptr,
                               const int32_t* indices, const float* data, const int64_t* offsets,
                               const int32_t* lengths, const uint32_t* block_starts,
                               int64_t total_padded, int32_t* doc_ids, float* weights,
                               float* max_scores, void* ws, int64_t ws_bytes, void* stream) {
-  int rc = check_csr_args(n_docs, V, block_docs, indptr);
+  GSP_REQUIRE(total_padded >= 0, GSP_ERR_ARG, "gsp_index_fill: total_padded < 0");
+  int rc = gsp_index_fill_chunk(n_docs, V, block_docs, 0, n_docs, indptr, indices, data, offsets,
+                                block_starts, doc_ids, weights, ws, ws_bytes, stream);
   if (rc) return rc;
-  cudaStream_t st = as_stream(stream);
-  const int64_t nb = n_blocks_of(n_docs, block_docs);
-  if (total_padded > 0) {
-    GSP_CUDA(cudaMemsetAsync(doc_ids, 0xFF, size_t(total_padded) * 4, st));
-    GSP_CUDA(cudaMemsetAsync(weights, 0, size_t(total_padded) * 4, st));
-  }
-  if (nb > 0) {
-    const size_t smem = size_t(V) * 2;
-    GSP_REQUIRE(smem <= size_t(max_smem_optin()), GSP_ERR_UNSUPPORTED,
-                "index build: vocabulary %d too large", V);
-    GSP_CUDA(cudaFuncSetAttribute(fill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    fill_kernel<<<unsigned(nb), 32, smem, st>>>(n_docs, V, block_docs, indptr, indices, data, offsets,
-                                                block_starts, doc_ids, weights);
-    GSP_CHECK_LAUNCH();
-  }
-  max_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, st>>>(V, offsets, lengths, weights,
-                                                                       max_scores);
-  GSP_CHECK_LAUNCH();
-  // a term listed twice in one document row would give one list a repeated doc id; the
-  // scorer applies a list's postings to distinct documents in parallel, so that is refused
-  GSP_REQUIRE(ws && ws_bytes >= 16, GSP_ERR_ARG, "gsp_index_fill: workspace too small");
-  unsigned long long* d_cnt = static_cast<unsigned long long*>(ws);
-  GSP_CUDA(cudaMemsetAsync(d_cnt, 0, 16, st));
-  check_sorted_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, st>>>(V, doc_ids, offsets,
-                                                                                 lengths, d_cnt);
-  GSP_CHECK_LAUNCH();
-  unsigned long long h[2] = {0, 0};
-  GSP_CUDA(cudaMemcpyAsync(h, d_cnt, 16, cudaMemcpyDeviceToHost, st));
-  GSP_CUDA(cudaStreamSynchronize(st));
-  GSP_REQUIRE(h[1] == 0, GSP_ERR_UNSORTED,
-              "index build: %llu terms occur twice in one document row (duplicate (doc, term) "
-              "entries); merge them first, e.g. scipy's csr_matrix.sum_duplicates()", h[1]);
-  return GSP_OK;
+  return gsp_index_fill_finish(n_docs, V, offsets, lengths, doc_ids, weights, max_scores, ws,
+                               ws_bytes, stream);
 }
 
 extern "C" int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t* offsets,

@@ -7,7 +7,8 @@ libgpusparse.so, reached through the C ABI of include/gpusparse.h.  No Triton, n
 fallback: every entry point raises if the library or a CUDA device is missing.
 """
 from .index import (BLOCK_DOCS, BLOCK_SIZE, VOCAB_SIZE, GPUInvertedIndex,  # noqa: F401
-                    build_from_csr_tensors, build_gpu_index_from_csr, build_gpu_inverted_index,
+                    build_from_csr_tensors, build_from_host_csr, build_gpu_index_from_csr,
+                    build_gpu_inverted_index, build_streamed,
                     build_gpu_inverted_index_from_sparse, build_index_from_scipy,
                     dequantized_weights, generate_synthetic_splade_data, index_memory_stats,
                     load_index, quantize_, save_index)

@@ -30,6 +30,8 @@ W_F32, W_BF16, W_U8 = 0, 1, 2
 EXPORTS = (
     "gsp_last_error", "gsp_version", "gsp_scan_i32", "gsp_scan_ws_bytes", "gsp_synth_nnz",
     "gsp_synth_fill", "gsp_index_ws_bytes", "gsp_index_count", "gsp_index_fill",
+    "gsp_index_count_chunk", "gsp_index_count_finish", "gsp_index_fill_chunk",
+    "gsp_index_fill_finish",
     "gsp_index_quantize", "gsp_index_head_rows", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
     "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_merge_topk",
     "gsp_compacted_ws_bytes", "gsp_compacted_topk",
@@ -83,6 +85,13 @@ def lib() -> ctypes.CDLL:
                                                ctypes.POINTER(i64), p, i64, p]),
             "gsp_index_fill": (ctypes.c_int, [i64, i32, i32, p, p, p, p, p, p, i64, p, p, p, p,
                                               i64, p]),
+            "gsp_index_count_chunk": (ctypes.c_int, [i64, i32, i32, i64, i64, p, p, p, p, i64,
+                                                     p]),
+            "gsp_index_count_finish": (ctypes.c_int, [i64, i32, i32, p, p, p, p,
+                                                      ctypes.POINTER(i64), p, i64, p]),
+            "gsp_index_fill_chunk": (ctypes.c_int, [i64, i32, i32, i64, i64, p, p, p, p, p, p, p,
+                                                    p, i64, p]),
+            "gsp_index_fill_finish": (ctypes.c_int, [i64, i32, p, p, p, p, p, p, i64, p]),
             "gsp_index_quantize": (ctypes.c_int, [i32, i64, p, p, p, p, i32, p, p, p]),
             "gsp_index_head_rows": (ctypes.c_int, [i32, p, p, p, p, p, i32, i64, p, p]),
             "gsp_check_sorted": (ctypes.c_int, [i32, p, p, p, ctypes.POINTER(i64),

@@ -15,7 +15,8 @@ keeps:
   0 where absent) that the scorer streams with coalesced vector loads into register
   accumulators instead of scattering their postings.
 
-Builders run on the GPU (csrc/build.cu); the CSR is only copied host -> device.
+Builders run on the GPU (csrc/build.cu); the CSR is only copied host -> device, in chunks
+of rows when it comes from the host (``build_from_host_csr``, ``build_streamed``).
 """
 from __future__ import annotations
 
@@ -80,10 +81,50 @@ def build_from_csr_tensors(indptr: torch.Tensor, indices: torch.Tensor, data: to
     indices = indices.to(device=device, dtype=torch.int32).contiguous()
     data = data.to(device=device, dtype=torch.float32).contiguous()
     N = indptr.numel() - 1
-    V = int(vocab_size)
+    return build_streamed(N, vocab_size, lambda lo, hi, with_data: (indptr, indices, data),
+                          device, chunk_docs=max(N, 1), weight_dtype=weight_dtype,
+                          doc_base=doc_base, keep_fp32=keep_fp32, block_docs=block_docs,
+                          head_ids=head_ids)
+
+
+def build_streamed(num_docs: int, vocab_size: int, get_chunk, device,
+                   chunk_docs: int = 1 << 21, weight_dtype: str = "fp32", doc_base: int = 0,
+                   keep_fp32: bool = True, block_docs: int = BLOCK_DOCS,
+                   head_ids=None) -> GPUInvertedIndex:
+    """Build from CSR rows delivered in chunks, so that only the index and one chunk of rows
+    are on the device at a time (a corpus whose CSR and index do not fit together).
+
+    ``get_chunk(lo, hi, with_data)`` returns ``(indptr, indices, data)`` for documents
+    [lo, hi): indptr has hi - lo + 1 entries indexing the returned indices/data; data may be
+    None when ``with_data`` is False.  Every chunk is requested twice, once for the count
+    pass (without data) and once for the fill pass, with the same bounds.  Chunks hold
+    ``chunk_docs`` documents (rounded down to whole ``block_docs`` blocks) except the last.
+    The result is identical to building from the whole CSR at once.
+    """
+    device = _dev(device)
+    N, V = int(num_docs), int(vocab_size)
     if V <= 0:
         raise ValueError("vocab_size must be positive")
+    if N < 0:
+        raise ValueError("num_docs must be >= 0")
+    step = N if chunk_docs >= N else max(block_docs, int(chunk_docs) // block_docs * block_docs)
+    bounds = [(lo, min(N, lo + step)) for lo in range(0, N, max(step, 1))]
     lib = L.lib()
+
+    def fetch(lo, hi, with_data):
+        ip, ix, dt = get_chunk(lo, hi, with_data)
+        ip = torch.as_tensor(ip).to(device=device, dtype=torch.int64).contiguous()
+        ix = torch.as_tensor(ix).to(device=device, dtype=torch.int32).contiguous()
+        if ip.numel() != hi - lo + 1:
+            raise ValueError(f"chunk [{lo}, {hi}): indptr has {ip.numel()} entries, "
+                             f"expected {hi - lo + 1}")
+        if with_data:
+            dt = torch.as_tensor(dt).to(device=device, dtype=torch.float32).contiguous()
+            if dt.numel() != ix.numel():
+                raise ValueError(f"chunk [{lo}, {hi}): {ix.numel()} indices but {dt.numel()} "
+                                 "weights")
+        return ip, ix, dt
+
     with torch.cuda.device(device):
         st = L.stream_of(device)
         nb = (N + block_docs - 1) // block_docs
@@ -92,19 +133,31 @@ def build_from_csr_tensors(indptr: torch.Tensor, indices: torch.Tensor, data: to
         padded = torch.empty(V, dtype=torch.int32, device=device)
         offsets = torch.empty(V, dtype=torch.int64, device=device)
         block_starts = torch.empty((nb + 1, V), dtype=torch.int32, device=device)
+        for lo, hi in bounds:
+            ip, ix, _ = fetch(lo, hi, False)
+            L.check(lib.gsp_index_count_chunk(N, V, block_docs, lo, hi - lo, L.ptr(ip), L.ptr(ix),
+                                              L.ptr(block_starts), L.ptr(ws), ws.numel(), st),
+                    "index build")
+            del ip, ix
         total = ctypes.c_int64(0)
-        L.check(lib.gsp_index_count(N, V, block_docs, L.ptr(indptr), L.ptr(indices),
-                                    L.ptr(lengths), L.ptr(padded), L.ptr(offsets),
-                                    L.ptr(block_starts), ctypes.byref(total), L.ptr(ws),
-                                    ws.numel(), st), "index build")
+        L.check(lib.gsp_index_count_finish(N, V, block_docs, L.ptr(lengths), L.ptr(padded),
+                                           L.ptr(offsets), L.ptr(block_starts),
+                                           ctypes.byref(total), L.ptr(ws), ws.numel(), st),
+                "index build")
         P = int(total.value)
         doc_ids = torch.empty(max(P, 0), dtype=torch.int32, device=device)
         scores = torch.empty(max(P, 0), dtype=torch.float32, device=device)
         max_scores = torch.empty(V, dtype=torch.float32, device=device)
-        L.check(lib.gsp_index_fill(N, V, block_docs, L.ptr(indptr), L.ptr(indices), L.ptr(data),
-                                   L.ptr(offsets), L.ptr(lengths), L.ptr(block_starts), P,
-                                   L.ptr(doc_ids), L.ptr(scores), L.ptr(max_scores), L.ptr(ws),
-                                   ws.numel(), st), "index build")
+        for lo, hi in bounds:
+            ip, ix, dt = fetch(lo, hi, True)
+            L.check(lib.gsp_index_fill_chunk(N, V, block_docs, lo, hi - lo, L.ptr(ip), L.ptr(ix),
+                                             L.ptr(dt), L.ptr(offsets), L.ptr(block_starts),
+                                             L.ptr(doc_ids), L.ptr(scores), L.ptr(ws),
+                                             ws.numel(), st), "index build")
+            del ip, ix, dt
+        L.check(lib.gsp_index_fill_finish(N, V, L.ptr(offsets), L.ptr(lengths), L.ptr(doc_ids),
+                                          L.ptr(scores), L.ptr(max_scores), L.ptr(ws),
+                                          ws.numel(), st), "index build")
         idx = GPUInvertedIndex(doc_ids=doc_ids, scores=scores, offsets=offsets, lengths=lengths,
                                padded_lengths=padded, max_scores=max_scores, num_docs=N,
                                vocab_size=V, device=device, block_starts=block_starts,
@@ -114,6 +167,23 @@ def build_from_csr_tensors(indptr: torch.Tensor, indices: torch.Tensor, data: to
         if block_docs == BLOCK_DOCS:
             ensure_head(idx, head_ids=head_ids)
     return idx
+
+
+def build_from_host_csr(indptr, indices, data, vocab_size: int, device,
+                        chunk_docs: int = 1 << 21, **kw) -> GPUInvertedIndex:
+    """Build from a host (numpy) CSR, copying it to the device one chunk of rows at a time."""
+    indptr = np.asarray(indptr, dtype=np.int64)
+
+    def get_chunk(lo, hi, with_data):
+        e0, e1 = int(indptr[lo]), int(indptr[hi])
+        ip = torch.from_numpy(indptr[lo:hi + 1] - e0)
+        ix = torch.from_numpy(np.ascontiguousarray(indices[e0:e1], dtype=np.int32))
+        dt = (torch.from_numpy(np.ascontiguousarray(data[e0:e1], dtype=np.float32))
+              if with_data else None)
+        return ip, ix, dt
+
+    return build_streamed(len(indptr) - 1, vocab_size, get_chunk, device, chunk_docs=chunk_docs,
+                          **kw)
 
 
 def quantize_(index: GPUInvertedIndex, weight_dtype: str, keep_fp32: bool = True) -> None:
@@ -297,17 +367,9 @@ def view(index: GPUInvertedIndex) -> L.IndexView:
 
 # ------------------------------------------------------------------ reference builders
 
-def _csr_to_device(indptr, indices, data, device):
-    device = _dev(device)
-    return (torch.as_tensor(np.ascontiguousarray(indptr, dtype=np.int64)).to(device),
-            torch.as_tensor(np.ascontiguousarray(indices, dtype=np.int32)).to(device),
-            torch.as_tensor(np.ascontiguousarray(data, dtype=np.float32)).to(device))
-
-
 def build_index_from_scipy(csr_mat, device, vocab_size: int, **kw) -> GPUInvertedIndex:
     csr = csr_mat.tocsr()
-    ip, ix, dt = _csr_to_device(csr.indptr, csr.indices, csr.data, device)
-    return build_from_csr_tensors(ip, ix, dt, vocab_size, device, **kw)
+    return build_from_host_csr(csr.indptr, csr.indices, csr.data, vocab_size, device, **kw)
 
 
 def build_gpu_index_from_csr(csr_mat, device, **kw) -> GPUInvertedIndex:
@@ -328,8 +390,7 @@ def build_gpu_inverted_index(doc_term_ids: list, doc_term_scores: list, vocab_si
             if len(lens) and indptr[-1] else np.zeros(0, dtype=np.float32))
     if indices.size and (indices.min() < 0 or indices.max() >= vocab_size):
         raise IndexError("term id outside [0, vocab_size)")
-    ip, ix, dt = _csr_to_device(indptr, indices.astype(np.int32), data, device)
-    return build_from_csr_tensors(ip, ix, dt, vocab_size, device, **kw)
+    return build_from_host_csr(indptr, indices.astype(np.int32), data, vocab_size, device, **kw)
 
 
 def build_gpu_inverted_index_from_sparse(sparse_matrix: torch.Tensor,

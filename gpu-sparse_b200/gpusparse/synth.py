@@ -21,7 +21,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
-from .index import GPUInvertedIndex, build_from_csr_tensors
+from .index import GPUInvertedIndex, build_streamed
 
 WTAB_SEGS = 65536
 GUIDE = 65536
@@ -140,11 +140,22 @@ def shard_range(num_docs: int, world: int, rank: int):
 
 def synth_index(num_docs: int, V: int = 30522, seed: int = 0, law: Law | None = None,
                 doc_range=None, device=None, weight_dtype: str = "fp32",
-                keep_fp32: bool = True, head_ids=None) -> GPUInvertedIndex:
-    """Index of documents [lo, hi) of the seeded corpus (local ids, doc_base = lo)."""
+                keep_fp32: bool = True, head_ids=None,
+                chunk_docs: int = 1 << 21) -> GPUInvertedIndex:
+    """Index of documents [lo, hi) of the seeded corpus (local ids, doc_base = lo).
+
+    The CSR is generated and consumed ``chunk_docs`` documents at a time (each chunk is
+    generated twice, for the count and the fill pass), so the device holds the index and
+    one chunk of rows, never the whole CSR."""
     lo, hi = doc_range if doc_range is not None else (0, num_docs)
-    ip, ix, dt = synth_csr(hi - lo, V, seed, kind=0, first=lo, law=law or DOC_LAW, device=device)
-    idx = build_from_csr_tensors(ip, ix, dt, V, ip.device, weight_dtype=weight_dtype, doc_base=lo,
-                                 keep_fp32=keep_fp32, head_ids=head_ids)
-    del ip, ix, dt
-    return idx
+    law = law or DOC_LAW
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+
+    def get_chunk(a, b, with_data):
+        return synth_csr(b - a, V, seed, kind=0, first=lo + a, law=law, device=dev)
+
+    return build_streamed(hi - lo, V, get_chunk, dev, chunk_docs=chunk_docs,
+                          weight_dtype=weight_dtype, doc_base=lo, keep_fp32=keep_fp32,
+                          head_ids=head_ids)

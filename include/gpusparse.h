@@ -73,7 +73,7 @@ int gsp_synth_fill(uint64_t seed, uint32_t kind, uint64_t first, int64_t n, int3
                    const int64_t* indptr, int32_t* indices, float* data, void* stream);
 
 /* ---------------------------------------------------------------- index build */
-/* Workspace bytes for gsp_index_count / gsp_index_fill on a CSR of n_docs rows. */
+/* Workspace bytes for the index build calls below on a CSR of n_docs rows. */
 int64_t gsp_index_ws_bytes(int64_t n_docs, int32_t V, int32_t block_docs);
 /* Pass 1 (replaces the argsort/bincount/cumsum of build_gpu_index_from_csr :47-58):
  * lengths, padded, offsets and block_starts on the device; *total_padded on the host
@@ -89,6 +89,35 @@ int gsp_index_fill(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t*
                    const int32_t* lengths, const uint32_t* block_starts, int64_t total_padded,
                    int32_t* doc_ids, float* weights, float* max_scores, void* ws,
                    int64_t ws_bytes, void* stream);
+/* Streamed build (no counterpart in the reference, whose builder needs the whole CSR on
+ * the device): the two passes above, split so that only one chunk of CSR rows is on the
+ * device at a time.  Order on one stream:
+ *   gsp_index_count_chunk for every chunk (the chunk at first_doc 0 first),
+ *   gsp_index_count_finish (synchronises; *total_padded sizes doc_ids/weights),
+ *   gsp_index_fill_chunk for every chunk with the same rows,
+ *   gsp_index_fill_finish (padding, max_scores, checks; synchronises).
+ * A chunk is documents [first_doc, first_doc + chunk_docs) of n_docs: first_doc a
+ * multiple of block_docs, chunk_docs too unless the chunk ends the corpus.  Its indptr
+ * has chunk_docs + 1 entries indexing its own indices/data (indptr[0] need not be 0).
+ * block_starts [n_blocks + 1, V] accumulates the counts of each block in place.  Writes
+ * stay inside each block's counted slice of a list: a chunk filled with more postings of
+ * a term than were counted is reported by gsp_index_fill_finish as GSP_ERR_ARG, and so
+ * are lists left out of order or with doc ids outside [0, n_docs) (e.g. a chunk never
+ * filled); a chunk filled with other rows of the same shape is not detectable. */
+int gsp_index_count_chunk(int64_t n_docs, int32_t V, int32_t block_docs, int64_t first_doc,
+                          int64_t chunk_docs, const int64_t* indptr, const int32_t* indices,
+                          uint32_t* block_starts, void* ws, int64_t ws_bytes, void* stream);
+int gsp_index_count_finish(int64_t n_docs, int32_t V, int32_t block_docs, int32_t* lengths,
+                           int32_t* padded, int64_t* offsets, uint32_t* block_starts,
+                           int64_t* total_padded, void* ws, int64_t ws_bytes, void* stream);
+int gsp_index_fill_chunk(int64_t n_docs, int32_t V, int32_t block_docs, int64_t first_doc,
+                         int64_t chunk_docs, const int64_t* indptr, const int32_t* indices,
+                         const float* data, const int64_t* offsets, const uint32_t* block_starts,
+                         int32_t* doc_ids, float* weights, void* ws, int64_t ws_bytes,
+                         void* stream);
+int gsp_index_fill_finish(int64_t n_docs, int32_t V, const int64_t* offsets,
+                          const int32_t* lengths, int32_t* doc_ids, float* weights,
+                          float* max_scores, void* ws, int64_t ws_bytes, void* stream);
 /* fp32 weights -> bf16 (round to nearest even) or uint8 impacts with per-term scale
  * max_scores[t] / 255 (q = clamp(rint(w / scale), 0, 255)). */
 int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t* offsets,

@@ -152,3 +152,54 @@ def test_chunk_bounds_and_unsorted_error():
     idx.doc_ids[o:o + 2] = idx.doc_ids[o:o + 2].flip(0)
     with pytest.raises(ValueError):
         gpusparse.build_chunk_boundaries(idx, 512)
+
+
+def _same_index(a, b):
+    for f in ("doc_ids", "offsets", "lengths", "padded_lengths", "block_starts", "head_ids",
+              "head_slot"):
+        assert torch.equal(getattr(a, f), getattr(b, f)), f
+    for f in ("scores", "max_scores", "head_rows"):
+        assert torch.equal(getattr(a, f).view(torch.int32), getattr(b, f).view(torch.int32)), f
+    assert (a.num_docs, a.doc_base, a.block_docs) == (b.num_docs, b.doc_base, b.block_docs)
+
+
+@pytest.mark.parametrize("chunk_docs", [1024, 3 * 1024, 5000])
+def test_streamed_build_equals_whole_csr(chunk_docs):
+    """Counting and filling chunk by chunk gives the same index, bit for bit, as one pass
+    over the whole CSR (5000 rounds down to whole 1024-document blocks)."""
+    from gpusparse import synth
+    N = 20_000
+    whole = synth.synth_index(N, seed=2, device=DEV, chunk_docs=1 << 30)
+    _same_index(whole, synth.synth_index(N, seed=2, device=DEV, chunk_docs=chunk_docs))
+    shard = synth.synth_index(N, seed=2, doc_range=(7168, N), device=DEV, chunk_docs=1 << 30)
+    _same_index(shard, synth.synth_index(N, seed=2, doc_range=(7168, N), device=DEV,
+                                         chunk_docs=chunk_docs))
+
+
+def test_host_csr_streamed_build_equals_oracle():
+    import gpusparse
+    N, V = 9000, 30522
+    ip, ix, dt = O.synth_csr(N, V, seed=4)
+    idx = gpusparse.build_from_host_csr(ip, ix, dt, V, DEV, chunk_docs=2048)
+    ref = O.build_index(ip, ix, dt, V)
+    for f in ("doc_ids", "scores", "offsets", "lengths", "padded_lengths", "max_scores"):
+        assert np.array_equal(getattr(idx, f).cpu().numpy(), getattr(ref, f)), f
+    t = lambda a: torch.from_numpy(a).to(DEV)  # noqa: E731
+    _same_index(idx, gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), V, DEV))
+
+
+def test_streamed_build_refuses_rows_other_than_counted():
+    """The fill pass of chunk [1024, 2048) is handed the rows of documents [0, 1024): every
+    write stays inside its block's counted slice of a list, and the surplus is reported."""
+    from gpusparse.index import build_streamed
+    N, V = 4096, 30522
+    ip, ix, dt = O.synth_csr(N, V, seed=3)
+
+    def get_chunk(lo, hi, with_data):
+        src = 0 if (with_data and lo == 1024) else lo
+        e0, e1 = ip[src], ip[src + hi - lo]
+        return (torch.from_numpy(ip[src:src + hi - lo + 1] - e0), torch.from_numpy(ix[e0:e1]),
+                torch.from_numpy(dt[e0:e1]))
+
+    with pytest.raises(ValueError, match="other rows"):
+        build_streamed(N, V, get_chunk, DEV, chunk_docs=1024)

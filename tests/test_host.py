@@ -1,6 +1,7 @@
 """Host-side logic that needs no GPU: the C ABI library loads and exports every declared
 symbol, reference argument validation, plug-in helpers, shard layout, key decoding and
 the synthetic generator's law."""
+import ctypes
 import json
 import os
 import re
@@ -180,3 +181,23 @@ def test_index_view_layout_matches_the_header(tmp_path):
     assert int(got["size"]) == ctypes.sizeof(L.IndexView)
     for n in names:
         assert int(got[n]) == getattr(L.IndexView, n).offset, n
+
+
+def test_streamed_build_chunk_arguments_are_checked_on_the_host():
+    """A chunk must be a run of whole blocks inside the corpus and the workspace large
+    enough; these calls fail their argument checks before any device work (the pointers
+    they get are never dereferenced)."""
+    import gpusparse._lib as L
+    lib = L.lib()
+    N, V, bd = 5000, 30522, 1024
+    need = int(lib.gsp_index_ws_bytes(N, V, bd))
+    ws = ctypes.create_string_buffer(need)
+    fake = ctypes.c_void_p(256)
+    for first, n, ws_bytes in [(100, 1024, need), (1024, 1000, need), (4096, 1000, need),
+                               (0, 1024, 8), (-1024, 1024, need)]:
+        rc = lib.gsp_index_count_chunk(N, V, bd, first, n, fake, fake, fake, ws, ws_bytes, None)
+        assert rc == L.GSP_ERR_ARG, (first, n, ws_bytes)
+        rc = lib.gsp_index_fill_chunk(N, V, bd, first, n, fake, fake, fake, fake, fake, fake,
+                                      fake, ws, ws_bytes, None)
+        assert rc == L.GSP_ERR_ARG, (first, n, ws_bytes)
+    assert b"whole" in lib.gsp_last_error() or b"workspace" in lib.gsp_last_error()
