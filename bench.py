@@ -344,11 +344,18 @@ def run_ours(args):
         gs, gi = (x.cpu().numpy() for x in out)
         cpu = cpu_sample(index, qi, qs, k, gs, gi, args.cpu_seconds)
 
+    sharing = None
     if world > 1:
+        from gpusparse.distributed import _BOARDS, release_threshold_boards, shared_thresholds_enabled
+        mapped = sum(len(b.peers[0]) for b in _BOARDS.values())
+        sharing = (f"on: union bound over {world} shards, {mapped} peer boards mapped"
+                   if shared_thresholds_enabled() else "off")
+        release_threshold_boards()
         dist.destroy_process_group()
     if rank != 0:
         return
-    launches_per_step = 3 if world == 1 else 4   # plan, score, shard merge (+ global merge)
+    # plan, score, candidate counts, shard merge (+ global merge)
+    launches_per_step = 4 if world == 1 else 5
     line = {
         "metric": METRIC,
         "value": B * K / (total_ms * 1e-3),
@@ -368,7 +375,8 @@ def run_ours(args):
                    "weights": wd, "parallelism": f"doc-range shards x{world}" +
                    (" + NCCL all-gather merge" if world > 1 else ""),
                    "l2": "inputs larger than L2 (index >> 126 MB); no flush",
-                   "index_build_s": round(build_s, 2)},
+                   "index_build_s": round(build_s, 2),
+                   **({"threshold_sharing": sharing} if sharing else {})},
         "gpu_launches": launches_per_step * K,
         "e2e": {"value": B * K / (e2e_ms * 1e-3), "unit": "queries/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},

@@ -155,3 +155,59 @@ extern "C" int gsp_scan_i32(const int32_t* in, int64_t n, int64_t* out, void* ws
   GSP_CHECK_LAUNCH();
   return GSP_OK;
 }
+
+// ---------------------------------------------------------------------------------------
+// Threshold boards: one uint64 key per query that other processes (the other doc-range
+// shards of a batch, one per GPU) raise through CUDA IPC mappings of it.  Allocated with
+// cudaMalloc so that the IPC handle covers exactly the board.
+extern "C" int gsp_board_alloc(int64_t n, uint64_t** board, void* ipc_handle) {
+  GSP_REQUIRE(n > 0 && board, GSP_ERR_ARG, "gsp_board_alloc: bad arguments");
+  void* p = nullptr;
+  GSP_CUDA(cudaMalloc(&p, size_t(n) * sizeof(uint64_t)));
+  if (cudaMemset(p, 0, size_t(n) * sizeof(uint64_t)) != cudaSuccess) {
+    cudaFree(p);
+    set_error("gsp_board_alloc: cudaMemset failed");
+    return GSP_ERR_CUDA;
+  }
+  if (ipc_handle) {
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+      cudaFree(p);
+      set_error("gsp_board_alloc: cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+      return GSP_ERR_CUDA;
+    }
+    static_assert(sizeof(h) == GSP_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(ipc_handle, &h, sizeof(h));
+  }
+  *board = static_cast<uint64_t*>(p);
+  return GSP_OK;
+}
+
+extern "C" int gsp_board_free(uint64_t* board) {
+  GSP_REQUIRE(board, GSP_ERR_ARG, "gsp_board_free: null board");
+  GSP_CUDA(cudaFree(board));
+  return GSP_OK;
+}
+
+extern "C" int gsp_board_open(const void* ipc_handle, uint64_t** board) {
+  GSP_REQUIRE(ipc_handle && board, GSP_ERR_ARG, "gsp_board_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  GSP_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  *board = static_cast<uint64_t*>(p);
+  return GSP_OK;
+}
+
+extern "C" int gsp_board_close(uint64_t* board) {
+  GSP_REQUIRE(board, GSP_ERR_ARG, "gsp_board_close: null board");
+  GSP_CUDA(cudaIpcCloseMemHandle(board));
+  return GSP_OK;
+}
+
+extern "C" int gsp_board_clear(uint64_t* board, int64_t n, void* stream) {
+  GSP_REQUIRE(board && n >= 0, GSP_ERR_ARG, "gsp_board_clear: bad arguments");
+  GSP_CUDA(cudaMemsetAsync(board, 0, size_t(n) * sizeof(uint64_t), as_stream(stream)));
+  return GSP_OK;
+}

@@ -80,6 +80,7 @@ constexpr int kHeadVec = kHeadPart / 128;   // float4 accumulators per lane per 
 constexpr int kLongRun = 32;      // tail windows at least this long are streamed on their own
 constexpr int kSpinLimit = 1 << 21;   // default polls of a bounded wait (about a second)
 constexpr int kCompactUnroll = 8;     // keys per lane loaded together by a compaction pass
+constexpr int kMaxPeers = 8;          // other shards' threshold boards one launch raises
 
 struct ScoreParams {
   const int32_t* doc_ids;
@@ -118,6 +119,15 @@ struct ScoreParams {
   unsigned long long* item_next;   // next work item (zeroed)
   int32_t* fault;              // a bounded wait ran out (zeroed)
   int32_t wait_limit;          // polls before a wait gives up
+  // Doc-range shards of one batch scored at the same time (n_shards > 1) share a bound:
+  // row s of every shard's board [n_shards, B] holds, per query, a key that shard s has at
+  // least kg = ceil(k / n_shards) candidates at or above.  The minimum over the rows is a
+  // lower bound of the k-th best key of the whole corpus (the shards hold n_shards * kg
+  // >= k keys at or above it), so every shard may drop candidates below it.
+  unsigned long long* board;                  // this shard's board (local memory)
+  unsigned long long* peer_thr[kMaxPeers];    // the other shards' boards (peer memory)
+  int32_t n_peers;                            // n_shards - 1
+  int32_t n_shards, shard, kg;
 };
 
 namespace {
@@ -241,11 +251,12 @@ struct WarpLayout {
   static constexpr int total = hist + 256 * 4;
 };
 
-// Radix-select the k-th largest key of buf[0..n) (n > k, keys distinct), keep exactly the
-// k largest in place (stable) and return the smallest key value that is kept-or-better.
-// The buffer is written by warps of other SMs, so it is read through L2 (ld.global.cg).
-__device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t k,
-                                 uint32_t* __restrict__ hist) {
+// Radix select over the distinct keys buf[0..n) (n >= k >= 1): returns a key value P such
+// that exactly k keys are >= P (P is the k-th largest key with its low bits cleared below
+// the digit that decided it).  The buffer is written by warps of other SMs, so it is read
+// through L2 (ld.global.cg).
+__device__ uint64_t warp_select(const uint64_t* __restrict__ buf, int32_t n, int32_t k,
+                                uint32_t* __restrict__ hist) {
   const int lane = lane_id();
   // All keys share the bytes above the highest bit where the smallest and largest differ;
   // the digit passes start below them.  Every pass issues kCompactUnroll loads per lane
@@ -329,6 +340,15 @@ __device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t 
     __syncwarp();
     if (cD == need) break;
   }
+  return prefix;
+}
+
+// Keep exactly the k largest keys of buf[0..n) (n > k, keys distinct) in place (stable)
+// and return the smallest key value that is kept-or-better.
+__device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t k,
+                                 uint32_t* __restrict__ hist) {
+  const int lane = lane_id();
+  const uint64_t prefix = warp_select(buf, n, k, hist);
   // stable in-place compaction of keys >= prefix (writes never pass the loaded chunks)
   int32_t out = 0;
   for (int32_t i0 = 0; i0 < n; i0 += 32 * kCompactUnroll) {
@@ -495,12 +515,14 @@ struct QueryBuf {
   int32_t* fault;
   int32_t cap, k;
   int32_t wait_limit;
+  int32_t kg;                  // > 0: also return the kg-th best key after a compaction
 };
 
 // Appends the tile's documents whose score reaches threshold key thr (marked in m) to a
 // query's candidate buffers, following the protocol described at the top of the file.
-// Called only for tiles with a candidate.
-__device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restrict__ acc, uint32_t span,
+// Called only for tiles with a candidate.  Returns 0, or, when this warp compacted and
+// qb.kg > 0, a key that at least qb.kg keys of the new keep list reach.
+__device__ __noinline__ uint64_t append_candidates(QueryBuf qb, const float* __restrict__ acc, uint32_t span,
                                                uint32_t dbase, uint32_t* __restrict__ hist, uint64_t thr,
                                                uint32_t m) {
   const int lane = lane_id();
@@ -509,7 +531,7 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
     const int32_t cnt = __popc(m);
     const int32_t incl = lane_scan(cnt);
     const int32_t total = __shfl_sync(FULL, incl, 31);
-    if (total == 0) return;
+    if (total == 0) return 0;
     // one atomic gives the reservation and the generation it belongs to
     unsigned long long word = 0;
     if (lane == 0) word = atomicAdd(qb.rg, (unsigned long long)total);
@@ -531,7 +553,7 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
       if (pos + total <= qb.cap) {
         __threadfence();
         if (lane == 0) atomicAdd(qb.done + bsel, total);
-        return;
+        return 0;
       }
       // this warp crossed the capacity of generation g0
       bool ok = true;
@@ -567,7 +589,9 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
         atomicExch(qb.cdone, int32_t(g0 + 1u));
       }
       __syncwarp();
-      return;
+      // the keep list is this warp's own writes until the next compaction, which waits for
+      // cdone; reading it here races with nothing
+      return qb.kg > 0 ? warp_select(keep, qb.k, qb.kg, hist) : 0ull;
     }
     // generation g0 is full: wait until its crossing warp opens the next one, then retry
     // against the raised threshold
@@ -576,7 +600,7 @@ __device__ __noinline__ void append_candidates(QueryBuf qb, const float* __restr
     ok = __shfl_sync(FULL, int(ok), 0) != 0;
     if (!ok) {
       if (lane == 0) atomicOr(qb.fault, 1);
-      return;
+      return 0;
     }
     thr = max(thr, uint64_t(__ldcg(qb.gthr)));
   }
@@ -660,6 +684,8 @@ score_kernel(const ScoreParams p) {
       }
       __syncwarp();
       const unsigned long long g_pub = __ldcg(p.gthr + q);   // consumed by the selection
+      unsigned long long bnd = ~0ull;                        // lane s: shard s's row
+      if (p.n_shards > 1 && lane < p.n_shards) bnd = __ldcg(p.board + int64_t(lane) * p.B + q);
 
       // 2. tail runs in ascending term id
       const uint32_t* __restrict__ brow = p.block_starts + int64_t(b) * kTileBlocksI * p.V;
@@ -761,7 +787,12 @@ score_kernel(const ScoreParams p) {
       // 3. fused selection: the documents whose score reaches the query's threshold go to
       // its candidate buffer (a superset of the keys >= threshold is harmless: only the k
       // largest survive the compactions and the merge)
-      const uint64_t thr = uint64_t(g_pub);
+      uint64_t thr = uint64_t(g_pub);
+      if (p.n_shards > 1) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) bnd = min(bnd, __shfl_xor_sync(FULL, bnd, o));
+        thr = max(thr, uint64_t(bnd));
+      }
 #pragma unroll
       for (int h = 0; h < kTile / kSel; ++h) {
         if (uint32_t(h * kSel) >= span) break;
@@ -769,8 +800,19 @@ score_kernel(const ScoreParams p) {
         const uint32_t m = mark_tile(acc + h * kSel, lane, sp, thr);
         if (__any_sync(FULL, m != 0u)) {
           QueryBuf qb{p.cand + int64_t(q) * 3 * p.cand_stride, p.cand_stride, p.gthr + q, p.rg + q,
-                      p.done + 2 * q, p.cdone + q, p.fault, p.cap, p.k, p.wait_limit};
-          append_candidates(qb, acc + h * kSel, sp, uint32_t(p.doc_base + d0i + h * kSel), hist, thr, m);
+                      p.done + 2 * q, p.cdone + q, p.fault, p.cap, p.k, p.wait_limit, p.kg};
+          const uint64_t pub =
+              append_candidates(qb, acc + h * kSel, sp, uint32_t(p.doc_base + d0i + h * kSel), hist, thr, m);
+          // this shard's row of every board: local, then the peers' (remote reductions over
+          // NVLink; nothing waits on them)
+          if (pub != 0ull) {
+            const int64_t slot = int64_t(p.shard) * p.B + q;
+            if (lane == 0) atomicMax(p.board + slot, (unsigned long long)pub);
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r) {
+              if (r < p.n_peers && lane == r + 1) atomicMax(p.peer_thr[r] + slot, (unsigned long long)pub);
+            }
+          }
         }
       }
     }
@@ -899,7 +941,8 @@ extern "C" int64_t gsp_score_ws_bytes(const gsp_index_view* ix, int64_t B, int64
 // Everything after the configuration: plan, scoring kernel, merge, with the workspace at ws.
 static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const float* qs, int64_t B,
                           int64_t W, const Cfg& c, float* out_scores, int64_t* out_ids,
-                          uint64_t* out_keys, void* ws, cudaStream_t st) {
+                          uint64_t* out_keys, void* ws, cudaStream_t st, uint64_t* board = nullptr,
+                          int32_t shard = 0, int32_t n_shards = 1, uint64_t* const* peers = nullptr) {
   int rc = GSP_OK;
   GSP_REQUIRE(ix->doc_ids && ix->weights && ix->offsets && ix->lengths && ix->block_starts &&
                   (ix->wdtype != GSP_W_U8 || ix->term_scale),
@@ -948,6 +991,19 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.counts = reinterpret_cast<int32_t*>(w + c.off_counts);
   p.item_next = reinterpret_cast<unsigned long long*>(z + align8(2 * B * 8 + 3 * B * 4));
   p.fault = reinterpret_cast<int32_t*>(p.item_next + 1);
+  GSP_REQUIRE(n_shards >= 1 && n_shards <= kMaxPeers + 1 && shard >= 0 && shard < n_shards &&
+                  (n_shards == 1 || (board && peers)),
+              GSP_ERR_ARG, "gsp_score_topk_shared: bad shard arguments (shard %d of %d, at most %d)", shard,
+              n_shards, kMaxPeers + 1);
+  p.board = reinterpret_cast<unsigned long long*>(board);
+  p.n_shards = n_shards;
+  p.shard = shard;
+  p.n_peers = n_shards - 1;
+  p.kg = n_shards > 1 ? int32_t((c.kk + n_shards - 1) / n_shards) : 0;
+  for (int r = 0; r < kMaxPeers; ++r) {
+    p.peer_thr[r] = r < p.n_peers ? reinterpret_cast<unsigned long long*>(peers[r]) : nullptr;
+    GSP_REQUIRE(r >= p.n_peers || p.peer_thr[r], GSP_ERR_ARG, "gsp_score_topk_shared: null peer board %d", r);
+  }
   GSP_CUDA(cudaMemsetAsync(z, 0, size_t(c.zero_bytes), st));
 
   const size_t plan_smem = size_t(c.npow2) * 8;
@@ -1023,6 +1079,21 @@ extern "C" int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const
   GSP_REQUIRE(ws && ws_bytes >= c.total, GSP_ERR_ARG, "gsp_score_topk: workspace too small (%lld < %lld)",
               (long long)ws_bytes, (long long)c.total);
   return score_with_cfg(ix, qi, qs, B, W, c, out_scores, out_ids, out_keys, ws, as_stream(stream));
+}
+
+extern "C" int gsp_score_topk_shared(const gsp_index_view* ix, const int32_t* qi, const float* qs,
+                                     int64_t B, int64_t W, int64_t k, float* out_scores,
+                                     int64_t* out_ids, uint64_t* out_keys, void* ws, int64_t ws_bytes,
+                                     uint64_t* board, int32_t shard, int32_t n_shards,
+                                     uint64_t* const* peer_boards, void* stream) {
+  Cfg c;
+  int rc = make_cfg(ix, B, W, k, c);
+  if (rc) return rc;
+  GSP_REQUIRE(ws && ws_bytes >= c.total, GSP_ERR_ARG,
+              "gsp_score_topk_shared: workspace too small (%lld < %lld)", (long long)ws_bytes,
+              (long long)c.total);
+  return score_with_cfg(ix, qi, qs, B, W, c, out_scores, out_ids, out_keys, ws, as_stream(stream), board,
+                        shard, n_shards, peer_boards);
 }
 
 // ---------------------------------------------------------------------------------------

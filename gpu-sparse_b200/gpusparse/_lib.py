@@ -33,7 +33,8 @@ EXPORTS = (
     "gsp_index_count_chunk", "gsp_index_count_finish", "gsp_index_fill_chunk",
     "gsp_index_fill_finish",
     "gsp_index_quantize", "gsp_index_head_rows", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
-    "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_merge_topk",
+    "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_score_topk_shared", "gsp_board_alloc",
+    "gsp_board_free", "gsp_board_open", "gsp_board_close", "gsp_board_clear", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_merge_topk",
     "gsp_compacted_ws_bytes", "gsp_compacted_topk",
 )
 
@@ -102,6 +103,13 @@ def lib() -> ctypes.CDLL:
                                               p, p, p, i64, p]),
             "gsp_score_topk_noalloc": (ctypes.c_int, [ctypes.POINTER(IndexView), p, p, i64, i64,
                                                       i64, p, p, p, p]),
+            "gsp_score_topk_shared": (ctypes.c_int, [ctypes.POINTER(IndexView), p, p, i64, i64,
+                                                     i64, p, p, p, p, i64, p, i32, i32, p, p]),
+            "gsp_board_alloc": (ctypes.c_int, [i64, ctypes.POINTER(p), p]),
+            "gsp_board_free": (ctypes.c_int, [p]),
+            "gsp_board_open": (ctypes.c_int, [p, ctypes.POINTER(p)]),
+            "gsp_board_close": (ctypes.c_int, [p]),
+            "gsp_board_clear": (ctypes.c_int, [p, i64, p]),
             "gsp_profile_enable": (ctypes.c_int, [ctypes.c_int]),
             "gsp_set_wait_limit": (ctypes.c_int, [ctypes.c_int32]),
             "gsp_get_wait_limit": (ctypes.c_int32, []),

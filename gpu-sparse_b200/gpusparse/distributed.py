@@ -5,20 +5,31 @@ documents [r*N/G, (r+1)*N/G) with local ids and doc_base = r*N/G, scores the ful
 batch against it and keeps its exact local top-k as packed uint64 keys
 (fkey(score) << 32 | ~global doc id).  One all_gather_into_tensor moves the G lists
 (B*k*8 bytes per rank) into every rank's memory, and the GPU merge kernel reduces the G*k
-candidates of each query to the exact global top-k (ties -> lower global doc id).  No
-device ever reads another GPU's memory directly.
+candidates of each query to the exact global top-k (ties -> lower global doc id).
+
+While the shards score, they share a threshold: every rank has a board of G rows (one key
+per query and shard, CUDA IPC-mapped into the other ranks).  After each compaction a
+shard writes into its row of every board, with remote atomics over NVLink, a key that at
+least ceil(k/G) of its candidates reach; the minimum over the G rows is then a lower bound
+of the corpus's k-th best key (the shards hold at least k candidates at or above it), so
+every shard drops candidates below it -- a bound no single shard's own k-th best reaches
+until it has seen the whole corpus.  Nothing waits on a peer, and the result is the same
+bit for bit (GSP_SHARED_THRESHOLDS=0 turns the sharing off).
 
 This replaces the reference's 2-GPU experiments, which merged shard results on the host
 (src/comprehensive_benchmark.py:416-489, src/run_remeasure_audit.py:164-186).
 """
 from __future__ import annotations
 
+import ctypes
+import os
 from dataclasses import dataclass
 from typing import List
 
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from .synth import shard_range
 
 
@@ -68,6 +79,107 @@ def gather_candidates(local_keys: torch.Tensor, k: int, group=None) -> torch.Ten
     return out.view(world, B, k)
 
 
+class ThresholdBoards:
+    """This rank's threshold boards and IPC mappings of every other rank's (collective:
+    every rank of the group constructs, uses and closes them together).
+
+    Two boards per rank, used by alternate batches.  A batch clears its own board on its
+    stream before scoring; a raise from another rank's previous batch can only target the
+    other board, because a rank starts a batch only after the previous batch's all-gather,
+    which no rank finishes before every rank's scoring kernel of that batch has ended.
+    Raises of the current batch that land before the clear are lost, which only weakens a
+    bound.  If a peer's board cannot be mapped, this rank raises only its own board."""
+
+    def __init__(self, device: torch.device, capacity: int, group=None):
+        """capacity: queries per batch the boards hold (G rows of capacity keys each)."""
+        lib = L.lib()
+        self.device, self.capacity, self.group = device, int(capacity), group
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        self.world, self.rank = world, rank
+        self.own: List[int] = []
+        self.peers: List[List[int]] = [[], []]
+        self.epoch = 0
+        hb = (ctypes.c_ubyte * (2 * 64))()
+        with torch.cuda.device(device):
+            for e in range(2):
+                ptr = ctypes.c_void_p()
+                L.check(lib.gsp_board_alloc(world * self.capacity, ctypes.byref(ptr),
+                                            ctypes.byref(hb, 64 * e)), "threshold board")
+                self.own.append(int(ptr.value))
+            mine = torch.tensor(list(hb), dtype=torch.uint8, device=device)
+            allh = torch.empty(world * 2 * 64, dtype=torch.uint8, device=device)
+            dist.all_gather_into_tensor(allh, mine, group=group)
+            allh = bytes(allh.cpu().numpy().tobytes())
+            opened = [[], []]
+            ok = True
+            for r in range(world):
+                if r == rank or not ok:
+                    continue
+                for e in range(2):
+                    h = (ctypes.c_ubyte * 64).from_buffer_copy(allh, (2 * r + e) * 64)
+                    ptr = ctypes.c_void_p()
+                    if lib.gsp_board_open(ctypes.byref(h), ctypes.byref(ptr)) != L.GSP_OK:
+                        ok = False
+                        break
+                    opened[e].append(int(ptr.value))
+            if ok:
+                self.peers = opened
+            else:
+                for e in range(2):
+                    for ptr in opened[e]:
+                        lib.gsp_board_close(ctypes.c_void_p(ptr))
+
+    def next(self, B: int):
+        """(own board, peer boards) for the next batch of B queries; clears the own board's
+        G rows of B keys on the current stream."""
+        e = self.epoch & 1
+        self.epoch += 1
+        L.check(L.lib().gsp_board_clear(ctypes.c_void_p(self.own[e]), self.world * int(B),
+                                        L.stream_of(self.device)), "threshold board")
+        return self.own[e], self.peers[e]
+
+    def close(self) -> None:
+        """Unmap the peers' boards and free this rank's (collective)."""
+        lib = L.lib()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            for e in range(2):
+                for ptr in self.peers[e]:
+                    lib.gsp_board_close(ctypes.c_void_p(ptr))
+            self.peers = [[], []]
+            dist.barrier(group=self.group)
+            for ptr in self.own:
+                lib.gsp_board_free(ctypes.c_void_p(ptr))
+            self.own = []
+
+
+_BOARDS = {}
+
+
+def _boards(device: torch.device, B: int, group) -> "ThresholdBoards":
+    key = (device.index, id(group))
+    b = _BOARDS.get(key)
+    if b is None or b.capacity < B:
+        if b is not None:
+            b.close()
+        b = ThresholdBoards(device, max(B, 4096), group)
+        _BOARDS[key] = b
+    return b
+
+
+def release_threshold_boards() -> None:
+    """Close every threshold board of this process (collective; call before
+    destroy_process_group)."""
+    for b in list(_BOARDS.values()):
+        b.close()
+    _BOARDS.clear()
+
+
+def shared_thresholds_enabled() -> bool:
+    return os.environ.get("GSP_SHARED_THRESHOLDS", "1") != "0"
+
+
 def sharded_score_topk(index, layout: ShardLayout, query_term_ids: torch.Tensor,
                        query_term_scores: torch.Tensor, top_k: int, group=None):
     """Exact global top-k of the batch over all shards; every rank gets the result."""
@@ -75,7 +187,17 @@ def sharded_score_topk(index, layout: ShardLayout, query_term_ids: torch.Tensor,
     k = min(int(top_k), layout.num_docs)
     if layout.world == 1:
         return score_topk(index, query_term_ids, query_term_scores, k)
-    _, _, keys = score_topk(index, query_term_ids, query_term_scores, k, with_keys=True)
+    if shared_thresholds_enabled():
+        dev = index.device if isinstance(index.device, torch.device) else torch.device(index.device)
+        boards = _boards(dev, int(query_term_ids.shape[0]), group)
+        own, peers = boards.next(int(query_term_ids.shape[0]))
+        if len(peers) == layout.world - 1:
+            _, _, keys = score_topk(index, query_term_ids, query_term_scores, k, with_keys=True,
+                                    board=own, shard=layout.rank, peer_boards=peers)
+        else:   # the peers' boards could not be mapped: score alone
+            _, _, keys = score_topk(index, query_term_ids, query_term_scores, k, with_keys=True)
+    else:
+        _, _, keys = score_topk(index, query_term_ids, query_term_scores, k, with_keys=True)
     allk = gather_candidates(keys, k, group)
     return merge_topk(allk, layout.list_counts(k), k)
 

@@ -49,11 +49,21 @@ def _prep_queries(index: GPUInvertedIndex, qi: torch.Tensor, qs: torch.Tensor):
 
 def score_topk(index: GPUInvertedIndex, query_term_ids: torch.Tensor,
                query_term_scores: torch.Tensor, top_k: int = 10, with_keys: bool = False,
-               out: Optional[Tuple[torch.Tensor, ...]] = None):
+               out: Optional[Tuple[torch.Tensor, ...]] = None, board: Optional[int] = None,
+               shard: int = 0, peer_boards=()):
     """Exact top-k of every query over the whole index (see module docstring).
 
     with_keys=True also returns the packed uint64 candidate keys (as int64) used by the
     multi-GPU merge.  ``out`` may pass preallocated (scores, ids[, keys]) tensors.
+
+    ``board`` (a device address, or a CUDA int64 tensor of n_shards * B entries) turns
+    this into shard ``shard`` of n_shards = len(peer_boards) + 1 doc-range shards scoring
+    the batch at the same time: row s of a board holds, per query, a key that shard s has
+    at least ceil(k / n_shards) candidates at or above; the minimum over the rows bounds
+    the corpus-wide k-th best key from below and lets every shard drop candidates early.
+    This call writes its own row of its board and of ``peer_boards`` (device addresses of
+    the other shards' boards) and never clears them.  The shard may return fewer than k
+    real entries; merging all shards' keys gives the exact corpus top-k.
     """
     if top_k < 1:
         raise ValueError("top_k must be >= 1")
@@ -78,9 +88,19 @@ def score_topk(index: GPUInvertedIndex, query_term_ids: torch.Tensor,
         if ws_bytes < 0:
             L.check(int(-ws_bytes), "score_topk")
         ws = L.workspace(ws_bytes, dev)
-        L.check(lib.gsp_score_topk(ctypes.byref(v), L.ptr(qi), L.ptr(qs), B, max(W, 1), k,
-                                   L.ptr(s_out), L.ptr(i_out), L.ptr(k_out), L.ptr(ws), ws_bytes,
-                                   L.stream_of(dev)), "score_topk")
+        if board is None:
+            L.check(lib.gsp_score_topk(ctypes.byref(v), L.ptr(qi), L.ptr(qs), B, max(W, 1), k,
+                                       L.ptr(s_out), L.ptr(i_out), L.ptr(k_out), L.ptr(ws),
+                                       ws_bytes, L.stream_of(dev)), "score_topk")
+        else:
+            addr = board.data_ptr() if isinstance(board, torch.Tensor) else int(board)
+            peers = [p.data_ptr() if isinstance(p, torch.Tensor) else int(p) for p in peer_boards]
+            arr = (ctypes.c_void_p * max(len(peers), 1))(*peers)
+            L.check(lib.gsp_score_topk_shared(ctypes.byref(v), L.ptr(qi), L.ptr(qs), B, max(W, 1),
+                                              k, L.ptr(s_out), L.ptr(i_out), L.ptr(k_out),
+                                              L.ptr(ws), ws_bytes, ctypes.c_void_p(addr),
+                                              int(shard), len(peers) + 1, arr,
+                                              L.stream_of(dev)), "score_topk")
     return (s_out, i_out, k_out) if with_keys else (s_out, i_out)
 
 

@@ -201,6 +201,37 @@ int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* qi, const fl
                            int64_t B, int64_t W, int64_t k, float* out_scores, int64_t* out_ids,
                            uint64_t* out_keys, void* stream);
 
+/* gsp_score_topk for shard `shard` of n_shards doc-range shards of one corpus that score
+ * the same batch at the same time, one per GPU (no counterpart in the reference, whose
+ * shards exchange nothing before the merge).  Every shard has a board [n_shards, B]
+ * (device, uint64 keys, row s = shard s) and peer_boards holds the other n_shards - 1
+ * shards' boards (usually IPC mappings of other GPUs' memory; host array of device
+ * pointers).  After each compaction a shard writes into its row of every board (atomic
+ * max) a key that at least ceil(k / n_shards) of its candidates reach; the minimum over
+ * the rows is then a lower bound of the corpus-wide k-th best key (the shards hold at
+ * least k candidates at or above it), and every shard drops candidates below it.  The
+ * call never clears a board (a row of 0 means "no bound yet"), nothing waits on a peer,
+ * and the merge of all shards' keys (gsp_merge_topk) is exactly the corpus top-k; a
+ * shard may return fewer than k' real entries (the rest are -inf / -1 / key 0).  A
+ * board must not hold rows from another batch.  n_shards <= 9; n_shards == 1 is
+ * gsp_score_topk. */
+int gsp_score_topk_shared(const gsp_index_view* ix, const int32_t* qi, const float* qs,
+                          int64_t B, int64_t W, int64_t k, float* out_scores, int64_t* out_ids,
+                          uint64_t* out_keys, void* ws, int64_t ws_bytes, uint64_t* board,
+                          int32_t shard, int32_t n_shards, uint64_t* const* peer_boards,
+                          void* stream);
+
+/* Threshold boards for gsp_score_topk_shared (no reference counterpart).  alloc: n zeroed
+ * uint64 on the current device (cudaMalloc) and, if ipc_handle is not NULL, its
+ * GSP_IPC_HANDLE_BYTES-byte CUDA IPC handle for the other processes; open / close map and
+ * unmap another process's board; clear zeroes n entries on a stream. */
+#define GSP_IPC_HANDLE_BYTES 64
+int gsp_board_alloc(int64_t n, uint64_t** board, void* ipc_handle);
+int gsp_board_free(uint64_t* board);
+int gsp_board_open(const void* ipc_handle, uint64_t** board);
+int gsp_board_close(uint64_t* board);
+int gsp_board_clear(uint64_t* board, int64_t n, void* stream);
+
 /* Timing of the scoring kernel itself (no reference counterpart; used by the benchmark
  * for its roofline figure): while enabled, every gsp_score_topk brackets its main kernel
  * launch with CUDA events on the caller's stream; collect synchronises on them and returns

@@ -1,7 +1,8 @@
 """The sharded scorer as separate processes, one per GPU, over NCCL (skipped with fewer
 than two GPUs): every rank builds the index of its own document range with the global
 head set, and the all-gathered, merged top-k must equal the CPU oracle over the whole
-corpus bit for bit."""
+corpus bit for bit, with the ranks sharing thresholds through IPC-mapped boards (over
+several batches, so both boards of each rank are used) and without."""
 import os
 import socket
 from datetime import timedelta
@@ -38,11 +39,22 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         lay = ShardLayout(N, world, rank)
         idx = synth.synth_index(N, V, seed=0, doc_range=(lay.lo, lay.hi), device=dev)
         ensure_head(idx, head_ids=global_head(idx, N_HEAD))
+        from gpusparse.distributed import release_threshold_boards
         qi, qs = synth.synth_queries(B, V, seed=1, device=dev)
         s, i = sharded_score_topk(idx, lay, qi, qs, K)
+        # further batches alternate the threshold boards and must repeat the result; one
+        # more without sharing thresholds too
+        for _ in range(3):
+            s2, i2 = sharded_score_topk(idx, lay, qi, qs, K)
+            assert torch.equal(s2.view(torch.int32), s.view(torch.int32)) and torch.equal(i2, i)
+        os.environ["GSP_SHARED_THRESHOLDS"] = "0"
+        s3, i3 = sharded_score_topk(idx, lay, qi, qs, K)
+        os.environ.pop("GSP_SHARED_THRESHOLDS")
+        assert torch.equal(s3.view(torch.int32), s.view(torch.int32)) and torch.equal(i3, i)
         torch.cuda.synchronize()
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), s=s.cpu().numpy(), i=i.cpu().numpy(),
                  head=idx.head_ids.cpu().numpy())
+        release_threshold_boards()
     finally:
         dist.destroy_process_group()
 
