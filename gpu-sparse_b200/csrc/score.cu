@@ -465,6 +465,23 @@ __device__ __forceinline__ uint32_t mark_tile(const float* __restrict__ acc, int
   const uint32_t thi = uint32_t(thr >> 32);
   const float ts = thi < 0x00800000u ? -INFINITY : fkey_inv(thi);
   uint32_t m = 0;
+  if (span >= uint32_t(kSel)) {
+    // a whole tile: set.ge gives an all-ones word per passing score, masked into its bit
+#pragma unroll
+    for (int i = 0; i < kSel / 128; ++i) {
+      const float4 v = *reinterpret_cast<const float4*>(acc + 128 * i + 4 * lane);
+      uint32_t r0, r1, r2, r3;
+      asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(r0) : "f"(v.x), "f"(ts));
+      asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(r1) : "f"(v.y), "f"(ts));
+      asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(r2) : "f"(v.z), "f"(ts));
+      asm("set.ge.u32.f32 %0, %1, %2;" : "=r"(r3) : "f"(v.w), "f"(ts));
+      m |= r0 & (1u << (4 * i));
+      m |= r1 & (2u << (4 * i));
+      m |= r2 & (4u << (4 * i));
+      m |= r3 & (8u << (4 * i));
+    }
+    return m;
+  }
 #pragma unroll
   for (int i = 0; i < kSel / 128; ++i) {
     const float4 v = *reinterpret_cast<const float4*>(acc + 128 * i + 4 * lane);
