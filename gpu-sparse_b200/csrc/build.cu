@@ -125,22 +125,26 @@ fill_kernel(int64_t n_docs, int32_t V, int32_t block_docs, int64_t first_doc,
   }
 }
 
-// One warp per term, after every posting is in place: writes the list's padding (doc id -1,
-// weight 0), its max weight (0 for an empty list), and counts lists that are out of order
-// or hold a doc id outside [0, n_docs) (n_bad[0]) and lists that repeat a doc id (n_bad[1]).
-__global__ void finish_kernel(int64_t n_docs, int32_t V, const int64_t* __restrict__ offsets,
-                              const int32_t* __restrict__ lengths, int32_t* __restrict__ doc_ids,
-                              float* __restrict__ weights, float* __restrict__ max_scores,
-                              unsigned long long* __restrict__ n_bad) {
-  const int32_t t = (int32_t)((int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
-  const int lane = lane_id();
-  if (t >= V) return;
+// One block per term, after every posting is in place: writes the list's padding (doc id
+// -1, weight 0), its max weight (0 for an empty list), and counts lists that are out of
+// order or hold a doc id outside [0, n_docs) (n_bad[0]) and lists that repeat a doc id
+// (n_bad[1]).  A block, not a warp, per term: the longest lists hold every document.
+constexpr int kFinishThreads = 256;
+__global__ void __launch_bounds__(kFinishThreads)
+finish_kernel(int64_t n_docs, int32_t V, const int64_t* __restrict__ offsets,
+              const int32_t* __restrict__ lengths, int32_t* __restrict__ doc_ids,
+              float* __restrict__ weights, float* __restrict__ max_scores,
+              unsigned long long* __restrict__ n_bad) {
+  __shared__ float s_max[kFinishThreads / 32];
+  __shared__ int s_bad[kFinishThreads / 32], s_dup[kFinishThreads / 32];
+  const int32_t t = blockIdx.x;
+  const int lane = lane_id(), wid = threadIdx.x >> 5;
   const int64_t o = offsets[t];
   const int32_t L = lengths[t];
   const int32_t P = (L + kPostingPad - 1) / kPostingPad * kPostingPad;
   float m = -INFINITY;
   bool bad = false, dup = false;
-  for (int32_t p = lane; p < L; p += 32) {
+  for (int32_t p = threadIdx.x; p < L; p += kFinishThreads) {
     m = fmaxf(m, weights[o + p]);
     const int32_t b = doc_ids[o + p];
     bad |= b < 0 || int64_t(b) >= n_docs;
@@ -150,15 +154,31 @@ __global__ void finish_kernel(int64_t n_docs, int32_t V, const int64_t* __restri
       dup |= b == a;
     }
   }
-  for (int32_t p = L + lane; p < P; p += 32) {
+  for (int32_t p = L + threadIdx.x; p < P; p += kFinishThreads) {
     doc_ids[o + p] = -1;
     weights[o + p] = 0.0f;
   }
 #pragma unroll
-  for (int s = 16; s; s >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, s));
-  if (lane == 0) max_scores[t] = L > 0 ? m : 0.0f;
-  if (__any_sync(FULL, bad) && lane == 0) atomicAdd(n_bad, 1ull);
-  if (__any_sync(FULL, dup) && lane == 0) atomicAdd(n_bad + 1, 1ull);
+  for (int sh = 16; sh; sh >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, sh));
+  const bool wbad = __any_sync(FULL, bad), wdup = __any_sync(FULL, dup);
+  if (lane == 0) {
+    s_max[wid] = m;
+    s_bad[wid] = wbad;
+    s_dup[wid] = wdup;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = -INFINITY;
+    int bb = 0, dd = 0;
+    for (int w = 0; w < kFinishThreads / 32; ++w) {
+      mm = fmaxf(mm, s_max[w]);
+      bb |= s_bad[w];
+      dd |= s_dup[w];
+    }
+    max_scores[t] = L > 0 ? mm : 0.0f;
+    if (bb) atomicAdd(n_bad, 1ull);
+    if (dd) atomicAdd(n_bad + 1, 1ull);
+  }
 }
 
 __global__ void quant_kernel(int32_t V, const int64_t* __restrict__ offsets,
@@ -388,8 +408,8 @@ extern "C" int gsp_index_fill_finish(int64_t n_docs, int32_t V, const int64_t* o
   GSP_CUDA(cudaMemsetAsync(d_cnt, 0, 16, st));
   int32_t herr = 0;
   GSP_CUDA(cudaMemcpyAsync(&herr, ws, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
-  finish_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, st>>>(
-      n_docs, V, offsets, lengths, doc_ids, weights, max_scores, d_cnt);
+  finish_kernel<<<unsigned(V), kFinishThreads, 0, st>>>(n_docs, V, offsets, lengths, doc_ids, weights,
+                                                        max_scores, d_cnt);
   GSP_CHECK_LAUNCH();
   unsigned long long h[2] = {0, 0};
   GSP_CUDA(cudaMemcpyAsync(h, d_cnt, 16, cudaMemcpyDeviceToHost, st));
