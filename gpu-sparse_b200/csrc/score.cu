@@ -27,6 +27,13 @@
 // Every wait is bounded; one that runs out records a fault, and the merge then reports
 // NaN scores instead of a result.
 //
+// Doc-range shards of one corpus scored at the same time (one per GPU) also share a
+// bound: after each compaction a shard writes into its row of every shard's board
+// (remote atomics over NVLink) a key that ceil(k / n_shards) of its kept keys reach, and
+// a tile's selection uses the minimum over the rows when it is higher than the query's
+// own threshold.  The shards together hold k keys at or above that minimum, so it is a
+// lower bound of the corpus-wide k-th key and dropping keys below it loses nothing.
+//
 // Per tile:
 //  1. head terms (the index's densest terms, stored as dense rows): the warp keeps the
 //     accumulators of one part of the tile in registers (512 documents, 16 per lane, with
