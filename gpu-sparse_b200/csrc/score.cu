@@ -88,6 +88,8 @@ constexpr int kLongRun = 32;      // tail windows at least this long are streame
 constexpr int kSpinLimit = 1 << 21;   // default polls of a bounded wait (about a second)
 constexpr int kCompactUnroll = 8;     // keys per lane loaded together by a compaction pass
 constexpr int kMaxPeers = 8;          // other shards' threshold boards one launch raises
+constexpr int kTreeMinK = 256;        // small-batch mode: smallest k' and most query-tiles
+constexpr int64_t kTreeMaxTiles = 24576;
 
 struct ScoreParams {
   const int32_t* doc_ids;
@@ -135,6 +137,11 @@ struct ScoreParams {
   unsigned long long* peer_thr[kMaxPeers];    // the other shards' boards (peer memory)
   int32_t n_peers;                            // n_shards - 1
   int32_t n_shards, shard, kg;
+  // Small batches: instead of the shared candidate buffers, every tile writes its exact
+  // top tile_k keys to tile_out [B, n_blocks, tile_k] (0 in unused slots) and a tree of
+  // merges reduces them (no atomics, no waits).
+  uint64_t* tile_out;
+  int32_t tile_k;
 };
 
 namespace {
@@ -630,6 +637,102 @@ __device__ __noinline__ uint64_t append_candidates(QueryBuf qb, const float* __r
   }
 }
 
+// The kk (<= span) largest keys of one tile's scores (acc[col] for col < span, document
+// dbase + col), written to out[0..kk) in column order, and zeros in out[kk..slots).  A
+// radix select over the order-preserving score bits finds the kk-th largest score; every
+// score above it is kept, and of the scores equal to it the lowest columns (the larger
+// keys) until kk are kept, so the kept keys are exactly the kk largest.
+__device__ __noinline__ void tile_topk(const float* __restrict__ acc, uint32_t span, uint32_t dbase,
+                                       int32_t kk, int32_t slots, uint32_t* __restrict__ hist,
+                                       uint64_t* __restrict__ out) {
+  const int lane = lane_id();
+  uint32_t u[kSel / 32];   // element 4 * i + j: column 128 * i + 4 * lane + j
+#pragma unroll
+  for (int i = 0; i < kSel / 128; ++i) {
+    const float4 v = *reinterpret_cast<const float4*>(acc + 128 * i + 4 * lane);
+    const uint32_t c = uint32_t(128 * i + 4 * lane);
+    u[4 * i + 0] = c + 0 < span ? fkey(v.x) : 0u;
+    u[4 * i + 1] = c + 1 < span ? fkey(v.y) : 0u;
+    u[4 * i + 2] = c + 2 < span ? fkey(v.z) : 0u;
+    u[4 * i + 3] = c + 3 < span ? fkey(v.w) : 0u;
+  }
+  uint32_t prefix = 0;
+  int32_t need = kk;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int j = lane; j < 256; j += 32) hist[j] = 0u;
+    __syncwarp();
+    const uint32_t pmask = shift == 24 ? 0u : (~0u << (shift + 8));
+#pragma unroll
+    for (int e = 0; e < kSel / 32; ++e) {
+      const bool live = (u[e] & pmask) == prefix;
+      const uint32_t dig = live ? ((u[e] >> shift) & 255u) : 0x100u;
+      const uint32_t peers = __match_any_sync(FULL, dig);
+      if (live && (peers & lanemask_lt()) == 0u) hist[dig] += __popc(peers);
+      __syncwarp();
+    }
+    // digit D with (count above D) < need <= (count above D) + hist[D]
+    int32_t sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sum += int32_t(hist[255 - 8 * lane - j]);
+    const int32_t incl = lane_scan(sum);
+    const int L = __ffs(__ballot_sync(FULL, incl >= need)) - 1;
+    int32_t above = incl - sum, D = 0;
+    if (lane == L) {
+      for (int j = 0; j < 8; ++j) {
+        const int bin = 255 - 8 * lane - j;
+        const int32_t c = int32_t(hist[bin]);
+        if (above + c >= need) {
+          D = bin;
+          break;
+        }
+        above += c;
+      }
+    }
+    D = __shfl_sync(FULL, D, L);
+    above = __shfl_sync(FULL, above, L);
+    need -= above;
+    prefix |= uint32_t(D) << shift;
+    __syncwarp();
+  }
+  // prefix is the kk-th largest score key; take every key above it and the first `need`
+  // equal to it in column order
+  int32_t base = 0, eq_seen = 0;
+#pragma unroll
+  for (int i = 0; i < kSel / 128; ++i) {
+    uint32_t gtm = 0, eqm = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      gtm |= uint32_t(u[4 * i + j] > prefix) << j;
+      eqm |= uint32_t(u[4 * i + j] == prefix && u[4 * i + j] != 0u) << j;
+    }
+    const int32_t neq = __popc(eqm);
+    const int32_t eq_incl = lane_scan(neq);
+    int32_t r = eq_seen + eq_incl - neq;
+    uint32_t take = gtm;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if ((eqm >> j) & 1u) {
+        if (r < need) take |= 1u << j;
+        ++r;
+      }
+    }
+    const int32_t nt = __popc(take);
+    const int32_t t_incl = lane_scan(nt);
+    int32_t o = base + t_incl - nt;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if ((take >> j) & 1u) {
+        const int32_t col = 128 * i + 4 * lane + j;
+        if (o < kk) out[o] = pack_key(acc[col], dbase + uint32_t(col));   // o < kk by construction
+        ++o;
+      }
+    }
+    base += __shfl_sync(FULL, t_incl, 31);
+    eq_seen += __shfl_sync(FULL, eq_incl, 31);
+  }
+  for (int32_t j = kk + lane; j < slots; j += 32) out[j] = 0ull;
+}
+
 // Final candidate counts of every query: the keep list (k once a compaction happened) and
 // the open buffer (its written keys); the other buffer was compacted into the keep list.
 __global__ void final_counts_kernel(int32_t B, int32_t k, const unsigned long long* __restrict__ rg,
@@ -643,8 +746,9 @@ __global__ void final_counts_kernel(int32_t B, int32_t k, const unsigned long lo
   counts[3 * q + 2] = b == 1 ? done[2 * q + 1] : 0;
 }
 
-// WT: posting weight type; HT: head row type (WT, or float rows for uint8 postings).
-template <typename WT, typename HT>
+// WT: posting weight type; HT: head row type (WT, or float rows for uint8 postings);
+// kTree: small-batch mode (per-tile top-k lists instead of the shared candidate buffers).
+template <typename WT, typename HT, bool kTree>
 __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 score_kernel(const ScoreParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -817,6 +921,12 @@ score_kernel(const ScoreParams p) {
         for (int o = 16; o; o >>= 1) bnd = min(bnd, __shfl_xor_sync(FULL, bnd, o));
         thr = max(thr, uint64_t(bnd));
       }
+      if constexpr (kTree) {
+        // small-batch mode (one selection pass per tile): the tile's own exact top-k
+        tile_topk(acc, span, uint32_t(p.doc_base + d0i), min(p.tile_k, int32_t(span)), p.tile_k, hist,
+                  p.tile_out + (int64_t(q) * p.n_blocks + b) * p.tile_k);
+        continue;
+      }
 #pragma unroll
       for (int h = 0; h < kTile / kSel; ++h) {
         if (uint32_t(h * kSel) >= span) break;
@@ -844,6 +954,8 @@ score_kernel(const ScoreParams p) {
 }
 
 struct Cfg {
+  bool tree = false;   // small-batch mode: per-tile top-k lists and a merge tree
+  int64_t off_tiles = 0, off_lv0 = 0, off_lv1 = 0;
   int npow2 = 0, cap = 0, smem = 0, ctas_per_sm = 0, grid = 0;
   int64_t ecap = 0, n_blocks = 0, n_iblocks = 0, kk = 0, stride = 0;
   int64_t off_nhe = 0, off_hh = 0, off_hw = 0, off_hs = 0, off_nruns = 0, off_rterm = 0, off_rb32 = 0,
@@ -853,6 +965,8 @@ struct Cfg {
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 std::atomic<int32_t> g_wait_limit{kSpinLimit};
+// largest per-tile list buffer (B x tiles x k keys) for which a batch takes the merge tree
+std::atomic<int64_t> g_tree_limit{int64_t(256) << 20};
 int64_t align8(int64_t x) { return (x + 7) / 8 * 8; }
 
 // Workspace layout of one call for the configured buffer capacity.
@@ -875,6 +989,12 @@ void set_layout(Cfg& c, int64_t B) {
   // cleared by every call: thresholds [B] u64, reservation words [B] u64, written
   // counters [B, 2], finished compactions [B], item counter u64, fault flag
   c.off_zero = o; c.zero_bytes = align8(2 * B * 8 + 3 * B * 4) + 16; o = align256(o + c.zero_bytes);
+  if (c.tree) {
+    const int64_t g1 = (c.n_blocks + 7) / 8;
+    c.off_tiles = o; o = align256(o + B * c.n_blocks * c.kk * 8);
+    c.off_lv0 = o; o = align256(o + B * g1 * c.kk * 8);
+    c.off_lv1 = o; o = align256(o + B * ((g1 + 7) / 8) * c.kk * 8);
+  }
   c.total = o;
 }
 
@@ -908,6 +1028,14 @@ int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) 
   // pass's candidates.  Small buffers compact more often and so raise the threshold
   // sooner, which measured slightly faster than larger ones.
   c.cap = int(((c.kk + std::max<int64_t>(kSel, c.kk / 2) + 31) / 32) * 32);
+  // Small batches spread every query over thousands of warps that would all append to one
+  // candidate buffer, so the shared buffers serialise on its compactions; there each tile
+  // keeps its own top-k instead and a merge tree reduces the lists.
+  // Measured on B200: the tree wins for k' of a few hundred and more while B x tiles stays
+  // within a few times the number of warps (~24K); for small k' the shared buffers'
+  // compactions are short anyway.
+  c.tree = kTile == kSel && c.kk <= kSel && c.kk >= kTreeMinK && c.n_blocks > 0 && B > 0 &&
+           B * c.n_blocks <= kTreeMaxTiles && B * c.n_blocks * c.kk * 8 <= g_tree_limit.load();
   set_layout(c, B);
   return GSP_OK;
 }
@@ -927,7 +1055,7 @@ Profile& profile() {
 
 template <typename WT, typename HT>
 int launch_score(const ScoreParams& p, const Cfg& c, cudaStream_t st) {
-  auto kern = score_kernel<WT, HT>;
+  auto kern = c.tree ? score_kernel<WT, HT, true> : score_kernel<WT, HT, false>;
   if (int rc = ensure_smem(reinterpret_cast<const void*>(kern), c.smem)) return rc;
   Profile& pr = profile();
   std::pair<cudaEvent_t, cudaEvent_t>* evp = nullptr;
@@ -1024,6 +1152,8 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.shard = shard;
   p.n_peers = n_shards - 1;
   p.kg = n_shards > 1 ? int32_t((c.kk + n_shards - 1) / n_shards) : 0;
+  p.tile_out = c.tree ? reinterpret_cast<uint64_t*>(w + c.off_tiles) : nullptr;
+  p.tile_k = int32_t(c.kk);
   for (int r = 0; r < kMaxPeers; ++r) {
     p.peer_thr[r] = r < p.n_peers ? reinterpret_cast<unsigned long long*>(peers[r]) : nullptr;
     GSP_REQUIRE(r >= p.n_peers || p.peer_thr[r], GSP_ERR_ARG, "gsp_score_topk_shared: null peer board %d", r);
@@ -1054,6 +1184,22 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
     }
     if (rc) return rc;
   }
+  if (c.tree) {
+    // merge tree over the per-tile lists: 8 lists per node, the last level into the output
+    const uint64_t* in = p.tile_out;
+    int32_t n_in = int32_t(c.n_blocks);
+    uint64_t* lv[2] = {reinterpret_cast<uint64_t*>(w + c.off_lv0), reinterpret_cast<uint64_t*>(w + c.off_lv1)};
+    for (int level = 0;; ++level) {
+      const int32_t groups = (n_in + 7) / 8;
+      const bool last = groups == 1;
+      uint64_t* out = last ? out_keys : lv[level & 1];
+      rc = merge_tree_level(in, B, n_in, int32_t(c.kk), c.kk, last ? out_scores : nullptr,
+                            last ? out_ids : nullptr, out, st, -1);
+      if (rc || last) return rc;
+      in = out;
+      n_in = groups;
+    }
+  }
   final_counts_kernel<<<unsigned((B + 255) / 256), 256, 0, st>>>(int32_t(B), int32_t(c.kk), p.rg, p.done,
                                                                  p.cdone, p.counts);
   GSP_CHECK_LAUNCH();
@@ -1068,6 +1214,14 @@ extern "C" int gsp_set_wait_limit(int32_t polls) {
 }
 
 extern "C" int32_t gsp_get_wait_limit(void) { return g_wait_limit.load(); }
+
+extern "C" int gsp_set_tree_limit(int64_t bytes) {
+  GSP_REQUIRE(bytes >= 0, GSP_ERR_ARG, "gsp_set_tree_limit: negative limit");
+  g_tree_limit.store(bytes);
+  return GSP_OK;
+}
+
+extern "C" int64_t gsp_get_tree_limit(void) { return g_tree_limit.load(); }
 
 extern "C" int gsp_profile_enable(int on) {
   Profile& pr = profile();
@@ -1170,6 +1324,10 @@ extern "C" int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* q
   // a smaller candidate capacity means more frequent compactions, never another result;
   // the smallest one keeps k keys plus a whole tile
   const int min_cap = int(((c.kk + kSel + 31) / 32) * 32);
+  if (c.tree) {   // the per-tile lists would not fit the fixed scratch: shared buffers only
+    c.tree = false;
+    set_layout(c, B);
+  }
   while (c.total > int64_t(kNoAllocScratchBytes) && c.cap > min_cap) {
     c.cap = std::max(min_cap, c.cap / 2 / 32 * 32);
     set_layout(c, B);

@@ -49,7 +49,7 @@ merge_kernel(const uint64_t* __restrict__ keys, int64_t stride_b, int64_t stride
              const int32_t* __restrict__ fault, const int32_t* __restrict__ counts_dev, int64_t cstride_b,
              const CountsParam cp, int32_t use_param, int32_t k, int32_t k_out, int32_t kpow2,
              int64_t pad_id, float* __restrict__ out_s, int64_t* __restrict__ out_i,
-             uint64_t* __restrict__ out_k) {
+             uint64_t* __restrict__ out_k, int32_t tree_groups, int32_t tree_n_in) {
   extern __shared__ uint64_t sk[];
   __shared__ uint32_t hist[256];
   __shared__ int32_t s_total, s_n, s_D, s_above, s_cD;
@@ -60,8 +60,8 @@ merge_kernel(const uint64_t* __restrict__ keys, int64_t stride_b, int64_t stride
   if (fault && *fault) {
     // the producer of the candidates reported a fault: no result
     for (int32_t j = tid; j < k_out; j += blockDim.x) {
-      out_s[ob + j] = __int_as_float(0x7fc00000);
-      out_i[ob + j] = -1;
+      if (out_s) out_s[ob + j] = __int_as_float(0x7fc00000);
+      if (out_i) out_i[ob + j] = -1;
       if (out_k) out_k[ob + j] = 0ull;
     }
     return;
@@ -74,6 +74,13 @@ merge_kernel(const uint64_t* __restrict__ keys, int64_t stride_b, int64_t stride
   L.b = b;
   L.base = keys + int64_t(b) * stride_b;
   L.n = R;
+  if (tree_groups > 0) {
+    // one level of a merge tree: row b merges lists g*R .. g*R+R-1 (those that exist) of
+    // the tree_n_in lists of its query, stored one after another
+    const int32_t g = b % tree_groups;
+    L.base = keys + (int64_t(b / tree_groups) * tree_n_in + int64_t(g) * R) * stride_r;
+    L.n = min(R, tree_n_in - g * R);
+  }
 
   int32_t part = 0;
   for (int32_t r = tid; r < L.n; r += blockDim.x) part += L.count(r, cp);
@@ -168,8 +175,9 @@ merge_kernel(const uint64_t* __restrict__ keys, int64_t stride_b, int64_t stride
   const int32_t n = min(s_n, kpow2);
   for (int32_t i = n + tid; i < kpow2; i += blockDim.x) sk[i] = 0ull;
   __syncthreads();
-  // bitonic sort, descending
-  for (int32_t size = 2; size <= kpow2; size <<= 1) {
+  // bitonic sort, descending (an inner level of a merge tree passes its keys on unsorted)
+  const bool sort = out_s != nullptr || out_i != nullptr || tree_groups == 0;
+  for (int32_t size = 2; sort && size <= kpow2; size <<= 1) {
     for (int32_t stride = size >> 1; stride > 0; stride >>= 1) {
       for (int32_t i = tid; i < kpow2; i += blockDim.x) {
         const int32_t j = i ^ stride;
@@ -186,16 +194,16 @@ merge_kernel(const uint64_t* __restrict__ keys, int64_t stride_b, int64_t stride
     }
   }
   for (int32_t j = tid; j < k_out; j += blockDim.x) {
-    if (j < kk && j < n) {
-      const uint64_t key = sk[j];
-      out_s[ob + j] = key_score(key);
-      out_i[ob + j] = int64_t(key_doc(key));
-      if (out_k) out_k[ob + j] = key;
+    // key 0 is no document (an unused slot of a candidate list): a pad like a missing one
+    const uint64_t key = (j < kk && j < n) ? sk[j] : 0ull;
+    if (key != 0ull) {
+      if (out_s) out_s[ob + j] = key_score(key);
+      if (out_i) out_i[ob + j] = int64_t(key_doc(key));
     } else {
-      out_s[ob + j] = -INFINITY;
-      out_i[ob + j] = pad_id;
-      if (out_k) out_k[ob + j] = 0ull;
+      if (out_s) out_s[ob + j] = -INFINITY;
+      if (out_i) out_i[ob + j] = pad_id;
     }
+    if (out_k) out_k[ob + j] = key;
   }
 }
 
@@ -247,7 +255,30 @@ int merge_topk_device(const uint64_t* keys, int64_t B, int64_t R, int64_t stride
   merge_kernel<<<unsigned(B), kMergeThreads, smem, st>>>(keys, stride_b, stride_r, int32_t(R), fault,
                                                          counts_dev, cstride_b, cp, use_param, int32_t(k),
                                                          int32_t(k), kpow2, pad_id, out_scores, out_ids,
-                                                         out_keys);
+                                                         out_keys, 0, 0);
+  GSP_CHECK_LAUNCH();
+  return GSP_OK;
+}
+
+int merge_tree_level(const uint64_t* lists, int64_t B, int32_t n_in, int32_t slots, int64_t k,
+                     float* out_scores, int64_t* out_ids, uint64_t* out_keys, cudaStream_t st,
+                     int64_t pad_id) {
+  constexpr int32_t R = 8;
+  GSP_REQUIRE(B >= 0 && n_in >= 1 && slots >= 1 && k >= 1 && k <= kMaxK, GSP_ERR_ARG,
+              "merge tree: bad arguments");
+  const int32_t groups = (n_in + R - 1) / R;
+  const int64_t rows = B * groups;
+  GSP_REQUIRE(rows <= 0x7FFFFFFF, GSP_ERR_UNSUPPORTED, "merge tree: too many lists");
+  if (rows == 0) return GSP_OK;
+  CountsParam cp{};
+  for (int r = 0; r < R; ++r) cp.c[r] = slots;
+  int32_t kpow2 = 1;
+  while (kpow2 < k) kpow2 <<= 1;
+  const size_t smem = size_t(kpow2) * 8;
+  if (int rc = ensure_smem(reinterpret_cast<const void*>(merge_kernel), int(smem))) return rc;
+  merge_kernel<<<unsigned(rows), kMergeThreads, smem, st>>>(lists, 0, slots, R, nullptr, nullptr, 0, cp, 1,
+                                                            int32_t(k), int32_t(k), kpow2, pad_id, out_scores,
+                                                            out_ids, out_keys, groups, n_in);
   GSP_CHECK_LAUNCH();
   return GSP_OK;
 }

@@ -34,7 +34,7 @@ EXPORTS = (
     "gsp_index_fill_finish",
     "gsp_index_quantize", "gsp_index_head_rows", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
     "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_score_topk_shared", "gsp_board_alloc",
-    "gsp_board_free", "gsp_board_open", "gsp_board_close", "gsp_board_clear", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_merge_topk",
+    "gsp_board_free", "gsp_board_open", "gsp_board_close", "gsp_board_clear", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_set_tree_limit", "gsp_get_tree_limit", "gsp_merge_topk",
     "gsp_compacted_ws_bytes", "gsp_compacted_topk",
 )
 
@@ -113,6 +113,8 @@ def lib() -> ctypes.CDLL:
             "gsp_profile_enable": (ctypes.c_int, [ctypes.c_int]),
             "gsp_set_wait_limit": (ctypes.c_int, [ctypes.c_int32]),
             "gsp_get_wait_limit": (ctypes.c_int32, []),
+            "gsp_set_tree_limit": (ctypes.c_int, [i64]),
+            "gsp_get_tree_limit": (i64, []),
             "gsp_profile_collect": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double),
                                                    ctypes.POINTER(i64)]),
             "gsp_merge_topk": (ctypes.c_int, [p, i64, i64, i64, i64, p, i64, p, p, p, p]),

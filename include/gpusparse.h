@@ -245,6 +245,17 @@ int gsp_profile_enable(int on);
  * Applies to calls issued after it; process-wide. */
 int gsp_set_wait_limit(int32_t polls);
 int32_t gsp_get_wait_limit(void);
+
+/* Small-batch mode (no reference counterpart).  A batch with 256 <= k' <= 1024, at most
+ * 24576 (query, 1024-document tile) pairs and per-tile lists of at most `bytes`
+ * (B x ceil(n_docs / 1024) x k' x 8; default 256 MiB) skips the shared candidate
+ * buffers: every tile writes its own exact top-k' and a tree of merges (8 lists per
+ * node) reduces them, with no atomics and no waits.  That is faster when few queries
+ * spread over many tiles (their shared buffers would serialise on compactions).  Results
+ * are identical either way; 0 turns the mode off.  Applies to calls issued after it;
+ * process-wide.  gsp_score_ws_bytes accounts for it. */
+int gsp_set_tree_limit(int64_t bytes);
+int64_t gsp_get_tree_limit(void);
 int gsp_profile_collect(double* total_ms, int64_t* launches);
 
 /* ---------------------------------------------------------------- selection */

@@ -9,7 +9,7 @@ import torch
 from oracle import oracle as O
 from parity import assert_bit_exact
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("shared_buffers_only")]
 DEV = torch.device("cuda:0")
 V = 30522
 

@@ -39,11 +39,14 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         lay = ShardLayout(N, world, rank)
         idx = synth.synth_index(N, V, seed=0, doc_range=(lay.lo, lay.hi), device=dev)
         ensure_head(idx, head_ids=global_head(idx, N_HEAD))
+        import gpusparse._lib as L
         from gpusparse.distributed import release_threshold_boards
         qi, qs = synth.synth_queries(B, V, seed=1, device=dev)
-        s, i = sharded_score_topk(idx, lay, qi, qs, K)
-        # further batches alternate the threshold boards and must repeat the result; one
-        # more without sharing thresholds too
+        s, i = sharded_score_topk(idx, lay, qi, qs, K)     # small batch: per-tile lists
+        # the shared candidate buffers, whose compactions publish the shared bound: further
+        # batches alternate the threshold boards and must repeat the result; one more
+        # without sharing thresholds too
+        L.check(L.lib().gsp_set_tree_limit(0), "tree limit")
         for _ in range(3):
             s2, i2 = sharded_score_topk(idx, lay, qi, qs, K)
             assert torch.equal(s2.view(torch.int32), s.view(torch.int32)) and torch.equal(i2, i)

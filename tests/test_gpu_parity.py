@@ -219,3 +219,29 @@ def test_supported_limits_max_k_and_max_width(corpus, gindex):
     with pytest.raises(RuntimeError):
         gpusparse.triton_fused_score(gindex, t(np.zeros((2, 4097), np.int32)),
                                      t(np.zeros((2, 4097), np.float32)), top_k=10)
+
+
+@pytest.mark.parametrize("N", [1, 4097, 20000])
+def test_small_batch_merge_tree_matches_oracle(N):
+    """Small batches with k' >= 256 take the per-tile top-k lists and the merge tree; the
+    result is bit-exact against the oracle and equal to the shared-buffer path (forced by
+    a tree limit of 0)."""
+    import gpusparse
+    import gpusparse._lib as L
+    lib = L.lib()
+    ip, ix, dt = O.synth_csr(N, V, seed=N + 3)
+    oidx = O.build_index(ip, ix, dt, V)
+    g = gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), V, DEV)
+    default = lib.gsp_get_tree_limit()
+    try:
+        for B, k in [(1, 256), (3, 1000), (2, 1024), (6, 300)]:
+            qi, qs = O.synth_queries(B, V, seed=B * 7 + N)
+            s1, i1 = gpusparse.triton_fused_score(g, t(qi), t(qs), top_k=k)
+            rs, ri = O.score_topk(oidx, qi, qs, k, head=hd(g))
+            assert_bit_exact(s1.cpu().numpy(), i1.cpu().numpy(), rs, ri)
+            L.check(lib.gsp_set_tree_limit(0), "tree limit")
+            s0, i0 = gpusparse.triton_fused_score(g, t(qi), t(qs), top_k=k)
+            L.check(lib.gsp_set_tree_limit(default), "tree limit")
+            assert torch.equal(i1, i0) and torch.equal(s1.view(torch.int32), s0.view(torch.int32))
+    finally:
+        lib.gsp_set_tree_limit(default)

@@ -10,7 +10,7 @@ import torch
 from oracle import oracle as O
 from parity import assert_bit_exact
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("shared_buffers_only")]
 DEV = torch.device("cuda:0")
 N, V, B = 60_000, 30522, 48
 

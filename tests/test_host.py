@@ -201,3 +201,17 @@ def test_streamed_build_chunk_arguments_are_checked_on_the_host():
                                       fake, ws, ws_bytes, None)
         assert rc == L.GSP_ERR_ARG, (first, n, ws_bytes)
     assert b"whole" in lib.gsp_last_error() or b"workspace" in lib.gsp_last_error()
+
+
+def test_tree_limit_knob_round_trips_on_the_host():
+    """The small-batch mode's size limit is a process-wide host setting (no device work)."""
+    import gpusparse._lib as L
+    lib = L.lib()
+    default = lib.gsp_get_tree_limit()
+    assert default == 256 << 20
+    try:
+        assert lib.gsp_set_tree_limit(0) == L.GSP_OK and lib.gsp_get_tree_limit() == 0
+        assert lib.gsp_set_tree_limit(-1) == L.GSP_ERR_ARG
+    finally:
+        lib.gsp_set_tree_limit(default)
+    assert lib.gsp_get_tree_limit() == default
