@@ -3,9 +3,12 @@
 One process per GPU (torchrun), NCCL over NVLink/NVSwitch.  Rank r holds the index of
 documents [r*N/G, (r+1)*N/G) with local ids and doc_base = r*N/G, scores the full query
 batch against it and keeps its exact local top-k as packed uint64 keys
-(fkey(score) << 32 | ~global doc id).  One all_gather_into_tensor moves the G lists
-(B*k*8 bytes per rank) into every rank's memory, and the GPU merge kernel reduces the G*k
-candidates of each query to the exact global top-k (ties -> lower global doc id).
+(fkey(score) << 32 | ~global doc id).  The batch is split into G blocks of queries: one
+all_to_all_single sends rank r every rank's keys of block r (B*k*8/G bytes per pair), the
+GPU merge kernel reduces the G*k candidates of each of its B/G queries to the exact
+global top-k (ties -> lower global doc id), and one all_gather per output (scores, ids)
+gives every rank the whole result -- each rank merges 1/G of the batch and receives
+about 1/G of what an all-gather of every candidate list would move.
 
 While the shards score, they share a threshold: every rank has a board of G rows (one key
 per query and shard, CUDA IPC-mapped into the other ranks).  After each compaction a
@@ -180,6 +183,36 @@ def shared_thresholds_enabled() -> bool:
     return os.environ.get("GSP_SHARED_THRESHOLDS", "1") != "0"
 
 
+def exchange_candidates(local_keys: torch.Tensor, k: int, group=None) -> torch.Tensor:
+    """One all_to_all_single of query blocks: each rank's [B, k_local] int64 keys,
+    zero-padded to [Bp, k] (Bp = B rounded up to a multiple of the world size), are cut
+    into world blocks of Bp/world queries; rank r receives block r of every rank, as
+    [world, Bp/world, k]."""
+    world = dist.get_world_size(group)
+    B, kl = local_keys.shape
+    Bp = -(-B // world) * world
+    if kl < k or Bp != B:
+        padded = torch.zeros((Bp, k), dtype=local_keys.dtype, device=local_keys.device)
+        padded[:B, :kl] = local_keys
+        local_keys = padded
+    local_keys = local_keys.contiguous()
+    out = torch.empty_like(local_keys)
+    dist.all_to_all_single(out, local_keys, group=group)
+    return out.view(world, Bp // world, k)
+
+
+def gather_results(scores: torch.Tensor, ids: torch.Tensor, B: int, group=None):
+    """Every rank's merged block [Bp/world, k] of scores and ids into the whole batch on
+    every rank (two all-gathers), cut back to B queries."""
+    world = dist.get_world_size(group)
+    bb, k = scores.shape
+    s_all = torch.empty((world * bb, k), dtype=scores.dtype, device=scores.device)
+    i_all = torch.empty((world * bb, k), dtype=ids.dtype, device=ids.device)
+    dist.all_gather_into_tensor(s_all, scores.contiguous(), group=group)
+    dist.all_gather_into_tensor(i_all, ids.contiguous(), group=group)
+    return s_all[:B], i_all[:B]
+
+
 def sharded_score_topk(index, layout: ShardLayout, query_term_ids: torch.Tensor,
                        query_term_scores: torch.Tensor, top_k: int, group=None):
     """Exact global top-k of the batch over all shards; every rank gets the result."""
@@ -198,8 +231,9 @@ def sharded_score_topk(index, layout: ShardLayout, query_term_ids: torch.Tensor,
             _, _, keys = score_topk(index, query_term_ids, query_term_scores, k, with_keys=True)
     else:
         _, _, keys = score_topk(index, query_term_ids, query_term_scores, k, with_keys=True)
-    allk = gather_candidates(keys, k, group)
-    return merge_topk(allk, layout.list_counts(k), k)
+    blk = exchange_candidates(keys, k, group)
+    s, i = merge_topk(blk, layout.list_counts(k), k)
+    return gather_results(s, i, int(query_term_ids.shape[0]), group)
 
 
 def decode_keys(keys: torch.Tensor):
