@@ -7,8 +7,10 @@
 A step scores one batch of queries against the whole corpus and returns the exact top-k
 (k = 1000) per query.  The corpus is a BASELINE config (default 2: 8.8M documents,
 batch 1000) generated on each GPU from the seeded synthetic SPLADE-shaped law; with N
-GPUs every rank builds the index of its own contiguous doc range and the per-shard top-k
-lists are merged after one NCCL all-gather.  Work per step is fixed as N grows (strong
+GPUs every rank builds the index of its own contiguous doc range, the ranks share a lower
+bound of each query's k-th best key while they score (IPC-mapped boards), and the
+per-shard top-k lists are exchanged by query blocks (one NCCL all-to-all), merged (each
+rank its B/N queries) and all-gathered.  Work per step is fixed as N grows (strong
 scaling).
 
 Reported:
@@ -377,7 +379,7 @@ def run_ours(args):
         "data": "synthetic (seeded SPLADE-shaped law of BASELINE.json; generated on device)",
         "config": {"workload": wl["name"], "num_docs": N, "batch": B, "k": k, "vocab": V,
                    "weights": wd, "parallelism": f"doc-range shards x{world}" +
-                   (" + NCCL all-gather merge" if world > 1 else ""),
+                   (" + NCCL all-to-all of query blocks, merge, all-gather" if world > 1 else ""),
                    "l2": "inputs larger than L2 (index >> 126 MB); no flush",
                    "index_build_s": round(build_s, 2),
                    **({"threshold_sharing": sharing} if sharing else {})},
