@@ -70,7 +70,9 @@ def global_head(index, n_head: int, group=None) -> torch.Tensor:
 
 def gather_candidates(local_keys: torch.Tensor, k: int, group=None) -> torch.Tensor:
     """All-gather each rank's [B, k_local] int64 keys, zero-padded to [B, k], into
-    [world, B, k] on every rank (one collective)."""
+    [world, B, k] on every rank (one collective): every rank can then merge the whole
+    batch itself.  sharded_score_topk uses the query-block exchange below instead, which
+    moves and merges 1/world of this per rank."""
     world = dist.get_world_size(group)
     B, kl = local_keys.shape
     if kl < k:
