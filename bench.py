@@ -1,7 +1,8 @@
 #!/usr/bin/env python3
 """Benchmark of the exact learned-sparse scoring path on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference|cusparse]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2]
+                    [--impl ours|reference|cusparse|spare]
     torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1: doc-range shards)
 
 A step scores one batch of queries against the whole corpus and returns the exact top-k
@@ -30,7 +31,10 @@ the GPU box): rank 0 only, the others exit immediately.
 
 --impl cusparse is a context line only (one GPU, rank 0): the library route on the same
 B200 -- cuSPARSE SpMM (torch.sparse.mm of the corpus CSR, in 2M-document chunks, with the
-dense [V, B] query matrix) followed by torch.topk with a running top-k.
+dense [V, B] query matrix) followed by torch.topk with a running top-k.  --impl spare is
+another context line: the SPARe-style loop of the reference's baselines
+(baselines/bench_spare_iterative.py:58-77) -- per query, one torch index_add_ per term into
+a dense accumulator, then torch.topk -- on a bounded sample of the batch.
 """
 from __future__ import annotations
 
@@ -65,7 +69,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference", "cusparse"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "cusparse", "spare"], default="ours")
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--num-docs", type=int, default=None)
     ap.add_argument("--batch", type=int, default=None)
@@ -533,6 +537,68 @@ def run_cusparse(args):
     emit(line)
 
 
+def run_spare(args):
+    """Context line: the SPARe-style iterative loop (one index_add_ per query term over the
+    term-major posting arrays, then torch.topk per query) on one GPU, timed on a bounded
+    sample of the batch's queries."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    from gpusparse import synth
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    wl = workload(args)
+    N, B, k = wl["num_docs"], wl["batch"], wl["k"]
+    dlaw = synth.Law(zipf_s=wl["zipf_s"])
+    qlaw = synth.Law(zipf_s=wl["zipf_s"], nnz_mean=30.0, nnz_sd=15.0, nnz_lo=5, nnz_hi=128,
+                     min_nnz_item0=107)
+    index = synth.synth_index(N, V, seed=0, law=dlaw, device=dev)
+    qi, qs = synth.synth_queries(B, V, seed=1, law=qlaw, device=dev)
+    off = index.offsets.cpu().tolist()
+    ln = index.lengths.cpu().tolist()
+    qi_h, qs_h = qi.cpu().tolist(), qs.cpu()
+    doc_ids, wts = index.doc_ids, index.scores
+
+    def one(b):
+        acc = torch.zeros(N, dtype=torch.float32, device=dev)
+        for j, t in enumerate(qi_h[b]):
+            if 0 <= t < V and ln[t] > 0:
+                s0, s1 = off[t], off[t] + ln[t]
+                acc.index_add_(0, doc_ids[s0:s1].long(), wts[s0:s1] * float(qs_h[b, j]))
+        return torch.topk(acc, k)
+
+    one(0)
+    torch.cuda.synchronize()
+    # size the sample to a few seconds per step
+    t0 = time.perf_counter()
+    one(1 % B)
+    torch.cuda.synchronize()
+    per_q = max(time.perf_counter() - t0, 1e-4)
+    nq = int(max(1, min(B, 3.0 / per_q)))
+    times = []
+    for s_ in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for b in range(nq):
+            one((s_ * nq + b) % B)
+        torch.cuda.synchronize()
+        if s_ >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    wall = sum(times)
+    line = {
+        "impl": "spare", "metric": METRIC, "value": nq * len(times) / wall, "unit": "queries/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * wall / len(times), "p50_ms": 1e3 * statistics.median(times),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded SPLADE-shaped law of BASELINE.json; generated on device)",
+        "config": {"workload": wl["name"], "num_docs": N, "batch": B, "k": k, "vocab": V,
+                   "route": "per query: torch index_add_ per term + torch.topk (host-timed)",
+                   "step_sample_queries": nq},
+    }
+    emit(line)
+
+
 _JSON_FD = None
 
 
@@ -553,6 +619,8 @@ def main():
         run_reference(args)
     elif args.impl == "cusparse":
         run_cusparse(args)
+    elif args.impl == "spare":
+        run_spare(args)
     else:
         run_ours(args)
 
