@@ -245,3 +245,16 @@ def test_small_batch_merge_tree_matches_oracle(N):
             assert torch.equal(i1, i0) and torch.equal(s1.view(torch.int32), s0.view(torch.int32))
     finally:
         lib.gsp_set_tree_limit(default)
+
+
+def test_empty_corpus_builds_and_scores_to_nothing():
+    """A CSR with no rows builds an index with no postings; scoring it returns [B, 0]."""
+    import gpusparse
+    ip = np.zeros(1, dtype=np.int64)
+    ix = np.zeros(0, dtype=np.int32)
+    dt = np.zeros(0, dtype=np.float32)
+    g = gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), V, DEV)
+    assert g.num_docs == 0 and int(g.lengths.sum()) == 0
+    qi, qs = O.synth_queries(4, V, seed=9)
+    s, i = gpusparse.triton_fused_score(g, t(qi), t(qs), top_k=10)
+    assert s.shape == (4, 0) and i.shape == (4, 0)
