@@ -51,9 +51,15 @@ int merge_topk_device(const uint64_t* keys, int64_t B, int64_t R, int64_t stride
                       const int32_t* counts_host, int64_t k, float* out_scores, int64_t* out_ids,
                       uint64_t* out_keys, cudaStream_t st, int64_t pad_id = -1,
                       const int32_t* fault = nullptr);
-// One level of a merge tree: every group of 8 consecutive lists (of `slots` keys each,
-// unused slots 0) of each of B queries, n_in lists per query, reduced to its k largest
-// keys; the output rows are B x ceil(n_in / 8), in order, k keys each.
+// Lists per node of the small-batch merge tree.
+#ifndef GSP_TREE_FAN_IN
+#define GSP_TREE_FAN_IN 8
+#endif
+constexpr int kTreeFanIn = GSP_TREE_FAN_IN;
+
+// One level of a merge tree: every group of kTreeFanIn consecutive lists (of `slots` keys
+// each, unused slots 0) of each of B queries, n_in lists per query, reduced to its k
+// largest keys; the output rows are B x ceil(n_in / kTreeFanIn), in order, k keys each.
 int merge_tree_level(const uint64_t* lists, int64_t B, int32_t n_in, int32_t slots, int64_t k,
                      float* out_scores, int64_t* out_ids, uint64_t* out_keys, cudaStream_t st,
                      int64_t pad_id);

@@ -990,10 +990,10 @@ void set_layout(Cfg& c, int64_t B) {
   // counters [B, 2], finished compactions [B], item counter u64, fault flag
   c.off_zero = o; c.zero_bytes = align8(2 * B * 8 + 3 * B * 4) + 16; o = align256(o + c.zero_bytes);
   if (c.tree) {
-    const int64_t g1 = (c.n_blocks + 7) / 8;
+    const int64_t g1 = (c.n_blocks + kTreeFanIn - 1) / kTreeFanIn;
     c.off_tiles = o; o = align256(o + B * c.n_blocks * c.kk * 8);
     c.off_lv0 = o; o = align256(o + B * g1 * c.kk * 8);
-    c.off_lv1 = o; o = align256(o + B * ((g1 + 7) / 8) * c.kk * 8);
+    c.off_lv1 = o; o = align256(o + B * ((g1 + kTreeFanIn - 1) / kTreeFanIn) * c.kk * 8);
   }
   c.total = o;
 }
@@ -1185,12 +1185,13 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
     if (rc) return rc;
   }
   if (c.tree) {
-    // merge tree over the per-tile lists: 8 lists per node, the last level into the output
+    // merge tree over the per-tile lists: kTreeFanIn lists per node, the last level into
+    // the output
     const uint64_t* in = p.tile_out;
     int32_t n_in = int32_t(c.n_blocks);
     uint64_t* lv[2] = {reinterpret_cast<uint64_t*>(w + c.off_lv0), reinterpret_cast<uint64_t*>(w + c.off_lv1)};
     for (int level = 0;; ++level) {
-      const int32_t groups = (n_in + 7) / 8;
+      const int32_t groups = (n_in + kTreeFanIn - 1) / kTreeFanIn;
       const bool last = groups == 1;
       uint64_t* out = last ? out_keys : lv[level & 1];
       rc = merge_tree_level(in, B, n_in, int32_t(c.kk), c.kk, last ? out_scores : nullptr,

@@ -263,7 +263,8 @@ int merge_topk_device(const uint64_t* keys, int64_t B, int64_t R, int64_t stride
 int merge_tree_level(const uint64_t* lists, int64_t B, int32_t n_in, int32_t slots, int64_t k,
                      float* out_scores, int64_t* out_ids, uint64_t* out_keys, cudaStream_t st,
                      int64_t pad_id) {
-  constexpr int32_t R = 8;
+  constexpr int32_t R = kTreeFanIn;
+  static_assert(kTreeFanIn <= kMaxParamCounts, "tree fan-in above the parameter counts");
   GSP_REQUIRE(B >= 0 && n_in >= 1 && slots >= 1 && k >= 1 && k <= kMaxK, GSP_ERR_ARG,
               "merge tree: bad arguments");
   const int32_t groups = (n_in + R - 1) / R;
