@@ -25,14 +25,14 @@ namespace {
 constexpr int kCountThreads = 512;
 
 __global__ void __launch_bounds__(kCountThreads)
-count_kernel(int64_t n_docs, int32_t V, int32_t block_docs, int64_t first_block,
-             const int64_t* __restrict__ indptr, const int32_t* __restrict__ indices,
-             uint32_t* __restrict__ counts, int32_t use_smem, int32_t* __restrict__ err) {
+count_kernel(int64_t n_docs, int32_t V, int32_t block_docs, const int64_t* __restrict__ indptr,
+             const int32_t* __restrict__ indices, uint32_t* __restrict__ counts, int32_t use_smem,
+             int32_t* __restrict__ err) {
   extern __shared__ uint32_t hist[];
   const int64_t b = blockIdx.x;               // block of this chunk (documents local to it)
   const int64_t d0 = b * block_docs;
   const int64_t d1 = min(d0 + block_docs, n_docs);
-  uint32_t* row = counts + (first_block + b) * int64_t(V);
+  uint32_t* row = counts + b * int64_t(V);    // counts: the chunk's first block row
   if (use_smem) {
     for (int32_t t = threadIdx.x; t < V; t += blockDim.x) hist[t] = 0u;
     __syncthreads();
@@ -334,7 +334,7 @@ extern "C" int gsp_index_count_chunk(int64_t n_docs, int32_t V, int32_t block_do
     GSP_CUDA(cudaMemsetAsync(rows, 0, size_t(nb) * V * 4, st));
   }
   count_kernel<<<unsigned(nb), kCountThreads, use_smem ? smem : 0, st>>>(
-      chunk_docs, V, block_docs, 0, indptr, indices, rows, use_smem, err);
+      chunk_docs, V, block_docs, indptr, indices, rows, use_smem, err);
   GSP_CHECK_LAUNCH();
   return GSP_OK;
 }
