@@ -335,6 +335,22 @@ def run_ours(args):
     h2d = qi.numel() * qi.element_size() + qs.numel() * qs.element_size()
     d2h = s0.numel() * s0.element_size() + i0.numel() * i0.element_size()
 
+    # ---- one query alone (after the timed region; small-batch latency, device time, p50)
+    lat1 = None
+    if world == 1:
+        q1, s1 = qi[1:2].contiguous(), qs[1:2].contiguous()   # query 0 is the forced 107+-term one
+        for _ in range(3):
+            step(q1, s1)
+        t1 = []
+        for _ in range(9):
+            a_, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_.record()
+            step(q1, s1)
+            b_.record()
+            torch.cuda.synchronize()
+            t1.append(a_.elapsed_time(b_))
+        lat1 = statistics.median(t1)
+
     # ---- roofline of the scoring kernel (this rank's shard)
     balg, post = bytes_alg(index, qi, B, min(k, index.num_docs), wd)
     balg = max_over_ranks(balg)
@@ -388,6 +404,9 @@ def run_ours(args):
                    "index_build_s": round(build_s, 2),
                    **({"threshold_sharing": sharing} if sharing else {})},
         "gpu_launches": launches_per_step * K,
+        **({"single_query_latency": {"batch": 1, "k": k, "p50_ms": lat1,
+                                     "note": "query 1 of the batch alone, device time"}}
+           if lat1 is not None else {}),
         "e2e": {"value": B * K / (e2e_ms * 1e-3), "unit": "queries/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
