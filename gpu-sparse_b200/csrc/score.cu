@@ -41,9 +41,10 @@
 //     with coalesced 16-byte loads: acc = fma(q_w, w, acc) for every document;
 //  2. the accumulators go to shared memory and the tail terms (all others), in ascending
 //     term id, are scattered into them: a run whose window is long (or that a query
-//     repeats) is streamed on its own, four 32-posting chunks in flight; consecutive short
-//     runs are flattened into full 32-lane chunks, and lanes that hit the same document
-//     (different terms) are applied in term order, one rank at a time (match_any);
+//     repeats) is streamed on its own, four 32-posting chunks in flight (two consecutive
+//     long runs of at most 64 postings share one such window); consecutive short runs are
+//     flattened into full 32-lane chunks, and lanes that hit the same document (different
+//     terms) are applied in term order, one rank at a time (match_any);
 //  3. every score becomes a packed key (order-preserving score bits << 32 | ~doc id:
 //     larger is better, ties go to the lower doc id) and the keys whose score reaches the
 //     query's threshold go to its candidate buffer.  A discarded key is beaten by k kept
@@ -434,6 +435,42 @@ __device__ __forceinline__ void run_window(const int32_t* __restrict__ pd, const
     }
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
+      if (uint32_t(col[u]) < span) acc[col[u]] = v[u];
+    }
+  }
+}
+
+// Two consecutive runs of one entry each and at most 64 postings each (A then B, in term
+// order): the loads of both (two chunks each) in flight together, then A's chunks applied,
+// then B's (A and B may share documents).
+template <typename WT>
+__device__ __forceinline__ void run_pair(const int32_t* __restrict__ pa, const WT* __restrict__ wa, float sa,
+                                         int32_t na, float qa, const int32_t* __restrict__ pb,
+                                         const WT* __restrict__ wb, float sb, int32_t nb, float qb,
+                                         int32_t d0i, uint32_t span, float* __restrict__ acc) {
+  const int lane = lane_id();
+  int32_t col[4];
+  float w[4], v[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int32_t i = 32 * (u & 1) + lane;
+    const bool a = u < 2;
+    col[u] = -1;
+    w[u] = 0.f;
+    if (i < (a ? na : nb)) {
+      col[u] = __ldg((a ? pa : pb) + i) - d0i;
+      w[u] = WDecode<WT>::get(a ? wa : wb, i, a ? sa : sb);
+    }
+  }
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const float q = hh == 0 ? qa : qb;
+#pragma unroll
+    for (int u = 2 * hh; u < 2 * hh + 2; ++u) v[u] = uint32_t(col[u]) < span ? acc[col[u]] : 0.f;
+#pragma unroll
+    for (int u = 2 * hh; u < 2 * hh + 2; ++u) v[u] = __fmaf_rn(q, w[u], v[u]);
+#pragma unroll
+    for (int u = 2 * hh; u < 2 * hh + 2; ++u) {
       if (uint32_t(col[u]) < span) acc[col[u]] = v[u];
     }
   }
@@ -898,6 +935,23 @@ score_kernel(const ScoreParams p) {
           const int32_t e0_l = __shfl_sync(FULL, e0, jl), ne_l = __shfl_sync(FULL, ne, jl);
           const float w0_l = __shfl_sync(FULL, w0, jl), sc_l = __shfl_sync(FULL, scale, jl);
           const int64_t base = (int64_t(b32_l) << 5) + lo_l;
+          if (ne_l == 1 && nl_n <= 64) {
+            // the next run, if it is long with one entry and nothing lies between: as a pair
+            const uint32_t after = act & ~((2u << jl) - 1u);
+            const int j2 = after ? __ffs(after) - 1 : 32;
+            if (j2 < 32 && ((lng >> j2) & 1u)) {
+              const int32_t n2 = __shfl_sync(FULL, n, j2), ne2 = __shfl_sync(FULL, ne, j2);
+              const uint32_t lo2 = __shfl_sync(FULL, lo, j2), b322 = __shfl_sync(FULL, b32, j2);
+              const float w02 = __shfl_sync(FULL, w0, j2), sc2 = __shfl_sync(FULL, scale, j2);
+              if (ne2 == 1 && n2 <= 64) {
+                const int64_t base2 = (int64_t(b322) << 5) + lo2;
+                run_pair<WT>(doc_ids + base, wts + base, sc_l, nl_n, w0_l, doc_ids + base2, wts + base2, sc2, n2,
+                             w02, d0i, span, acc);
+                c = j2 + 1;
+                continue;
+              }
+            }
+          }
           if (ne_l == 1) {
             run_window<WT, 1>(doc_ids + base, wts + base, sc_l, nl_n, d0i, span, acc, w0_l, 0.f, nullptr, 0);
           } else if (ne_l == 2) {
