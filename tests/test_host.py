@@ -215,3 +215,33 @@ def test_tree_limit_knob_round_trips_on_the_host():
     finally:
         lib.gsp_set_tree_limit(default)
     assert lib.gsp_get_tree_limit() == default
+
+
+def test_small_batch_mode_is_chosen_by_the_documented_rules():
+    """Workspace sizing (host-only) includes the per-tile lists exactly when the
+    small-batch mode applies: 256 <= k' <= 1024, at most 24576 query-tiles, lists within
+    the size limit."""
+    import ctypes
+    import gpusparse._lib as L
+    lib = L.lib()
+    v = L.IndexView()
+    v.n_docs, v.V, v.block_docs, v.wdtype, v.n_head = 8_800_000, 30522, 1024, 0, 0
+    tiles = (v.n_docs + 1023) // 1024
+
+    def ws(B, k):
+        n = lib.gsp_score_ws_bytes(ctypes.byref(v), B, 128, k)
+        assert n > 0, lib.gsp_last_error()
+        return n
+
+    lists = lambda B, k: B * tiles * k * 8  # noqa: E731
+    assert ws(1, 1000) >= lists(1, 1000)            # one query, k = 1000: tree
+    assert ws(2, 1000) >= lists(2, 1000)            # 17 188 query-tiles: tree
+    assert ws(4, 1000) < lists(4, 1000)             # 34 376 query-tiles: shared buffers
+    assert ws(1, 255) < lists(1, 255)               # k' below 256: shared buffers
+    assert ws(1, 2000) < lists(1, 1024)             # k' above one tile: shared buffers
+    default = lib.gsp_get_tree_limit()
+    try:
+        L.check(lib.gsp_set_tree_limit(lists(1, 1000) - 1), "tree limit")
+        assert ws(1, 1000) < lists(1, 1000)         # lists above the limit: shared buffers
+    finally:
+        lib.gsp_set_tree_limit(default)
