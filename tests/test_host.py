@@ -245,3 +245,29 @@ def test_small_batch_mode_is_chosen_by_the_documented_rules():
         assert ws(1, 1000) < lists(1, 1000)         # lists above the limit: shared buffers
     finally:
         lib.gsp_set_tree_limit(default)
+
+
+def test_shared_scoring_and_board_arguments_are_checked_on_the_host():
+    """Bad shard arguments and bad board calls fail their checks before any device work
+    (the pointers below are never dereferenced)."""
+    import ctypes
+    import gpusparse._lib as L
+    lib = L.lib()
+    fake = ctypes.c_void_p(256)
+    v = L.IndexView()
+    v.n_docs, v.V, v.block_docs, v.wdtype, v.n_head = 5000, 30522, 1024, 0, 0
+    for f in ("doc_ids", "weights", "offsets", "lengths", "block_starts"):
+        setattr(v, f, 256)
+    B, W, k = 4, 8, 10
+    nb = lib.gsp_score_ws_bytes(ctypes.byref(v), B, W, k)
+    ws = ctypes.create_string_buffer(int(nb))
+    peers = (ctypes.c_void_p * 9)(*([256] * 9))
+    for board, shard, n_shards in [(fake, 0, 10), (fake, 2, 2), (fake, -1, 2),
+                                   (ctypes.c_void_p(0), 0, 2)]:
+        rc = lib.gsp_score_topk_shared(ctypes.byref(v), fake, fake, B, W, k, fake, fake, None, ws,
+                                       nb, board, shard, n_shards, peers, None)
+        assert rc == L.GSP_ERR_ARG, (shard, n_shards)
+    out = ctypes.c_void_p()
+    assert lib.gsp_board_alloc(0, ctypes.byref(out), None) == L.GSP_ERR_ARG
+    assert lib.gsp_board_clear(None, 4, None) == L.GSP_ERR_ARG
+    assert lib.gsp_board_open(None, ctypes.byref(out)) == L.GSP_ERR_ARG
