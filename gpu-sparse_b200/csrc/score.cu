@@ -85,7 +85,7 @@ constexpr int kTileBlocksI = GSP_TILE_BLOCKS;
 constexpr int kHeadPart = kCtasPerSm >= 5 ? 256 : (kCtasPerSm >= 4 ? 512 : 1024);
 constexpr int kHeadParts = kTile / kHeadPart;
 constexpr int kHeadVec = kHeadPart / 128;   // float4 accumulators per lane per part
-constexpr int kLongRun = 32;      // tail windows at least this long are streamed on their own
+constexpr int kLongRun = 24;      // tail windows at least this long are streamed on their own
 constexpr int kSpinLimit = 1 << 21;   // default polls of a bounded wait (about a second)
 constexpr int kCompactUnroll = 8;     // keys per lane loaded together by a compaction pass
 constexpr int kMaxPeers = 8;          // other shards' threshold boards one launch raises
