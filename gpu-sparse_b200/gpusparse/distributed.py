@@ -90,8 +90,9 @@ class ThresholdBoards:
 
     Two boards per rank, used by alternate batches.  A batch clears its own board on its
     stream before scoring; a raise from another rank's previous batch can only target the
-    other board, because a rank starts a batch only after the previous batch's all-gather,
-    which no rank finishes before every rank's scoring kernel of that batch has ended.
+    other board, because a rank starts a batch only after the previous batch's exchange
+    (the all-to-all of candidate keys), which no rank finishes before every rank's scoring
+    kernel of that batch has ended.
     Raises of the current batch that land before the clear are lost, which only weakens a
     bound.  If a peer's board cannot be mapped, this rank raises only its own board."""
 
