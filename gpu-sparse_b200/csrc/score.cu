@@ -8,8 +8,9 @@
 // tiles at any moment (their postings and dense head rows stay in L2) and no warp idles
 // while items are left.  A tile is a whole number of index blocks (one, 1024 documents,
 // by default), so the window of every term's postings inside a tile is
-// [block_starts[first block][t], block_starts[last block + 1][t]) with no search.  The warp owns the tile's fp32 accumulators, so every (query, document) cell
-// has exactly one writer, and the result does not depend on which warp scored which item.
+// [block_starts[first block][t], block_starts[last block + 1][t]) with no search.  The
+// warp owns the tile's fp32 accumulators, so every (query, document) cell has exactly one
+// writer, and the result does not depend on which warp scored which item.
 //
 // Candidates.  Each query has two candidate buffers used in turn and a keep list of the k
 // best keys found so far, shared by all warps; a 64-bit word (generation << 32 | reserved
@@ -48,7 +49,9 @@
 //  3. every score becomes a packed key (order-preserving score bits << 32 | ~doc id:
 //     larger is better, ties go to the lower doc id) and the keys whose score reaches the
 //     query's threshold go to its candidate buffer.  A discarded key is beaten by k kept
-//     keys, so the final top-k (merge_kernel in select.cu) is exact.
+//     keys, so the final top-k (merge_kernel in select.cu) is exact.  In the small-batch
+//     mode (kTree) the tile instead writes its own exact top-k' to a list of its own, and
+//     a merge tree reduces the lists (no shared buffers, atomics or waits).
 // Each cell therefore accumulates acc = fma(q_w, d_w, acc) in a fixed order -- head terms
 // by term id, then tail terms by term id, a repeated term in query-slot order -- with one
 // fp32 rounding per fused multiply-add: bitwise reproducible, and equal to the CPU
