@@ -271,3 +271,15 @@ def test_shared_scoring_and_board_arguments_are_checked_on_the_host():
     assert lib.gsp_board_alloc(0, ctypes.byref(out), None) == L.GSP_ERR_ARG
     assert lib.gsp_board_clear(None, 4, None) == L.GSP_ERR_ARG
     assert lib.gsp_board_open(None, ctypes.byref(out)) == L.GSP_ERR_ARG
+
+
+def test_run_file_is_the_reference_text(tmp_path):
+    """write_run produces the reference's TREC lines ("qid Q0 docno rank score gpusparse",
+    ranks from 1, Python's float text) in a gzip stream any reader accepts."""
+    import gzip
+    from lsr_benchmark_engine import gpusparse_retrieval as P
+    results = [[("q1", 3.5, "d7"), ("q1", 1.25, "d2")], [], [("q2", 0.1 + 0.2, "d0")]]
+    P.write_run(results, tmp_path / "run.txt.gz")
+    lines = gzip.open(tmp_path / "run.txt.gz", "rt").read().splitlines()
+    assert lines == ["q1 Q0 d7 1 3.5 gpusparse", "q1 Q0 d2 2 1.25 gpusparse",
+                     f"q2 Q0 d0 1 {0.1 + 0.2} gpusparse"]
