@@ -654,15 +654,16 @@ __device__ __noinline__ uint64_t append_candidates(QueryBuf qb, const float* __r
       for (int32_t j = lane; j < qb.k; j += 32) keep[j] = __ldcg(buf + j);
       __syncwarp();
       __threadfence();
+      // the shared-bound key, read while this warp still owns the keep list: the next
+      // compaction of this query, which rewrites it, waits for the cdone below
+      const uint64_t pc = qb.kg > 0 ? warp_select(keep, qb.k, qb.kg, hist) : 0ull;
       if (lane == 0) {
         atomicMax(qb.gthr, (unsigned long long)t);
         __threadfence();
         atomicExch(qb.cdone, int32_t(g0 + 1u));
       }
       __syncwarp();
-      // the keep list is this warp's own writes until the next compaction, which waits for
-      // cdone; reading it here races with nothing
-      return qb.kg > 0 ? warp_select(keep, qb.k, qb.kg, hist) : 0ull;
+      return pc;
     }
     // generation g0 is full: wait until its crossing warp opens the next one, then retry
     // against the raised threshold
