@@ -5,6 +5,11 @@ builders, triton_fused_score, triton_chunked_score, build_chunk_boundaries,
 compacted_topk, triton_chunked_score_fused) backed by hand-written CUDA kernels in
 libgpusparse.so, reached through the C ABI of include/gpusparse.h.  No Triton, no CPU
 fallback: every entry point raises if the library or a CUDA device is missing.
+
+Beyond the reference: streamed index builds (build_streamed, build_from_host_csr),
+index persistence (save_index, load_index), a captured fixed-shape scorer
+(CapturedScorer), and, in gpusparse.distributed, doc-range sharding over the GPUs of a
+node.
 """
 from .index import (BLOCK_DOCS, BLOCK_SIZE, VOCAB_SIZE, GPUInvertedIndex,  # noqa: F401
                     build_from_csr_tensors, build_from_host_csr, build_gpu_index_from_csr,
