@@ -19,6 +19,8 @@
 // only one chunk of the CSR needs to be on the device at a time.
 #include "common.cuh"
 
+#include <algorithm>
+
 namespace gsp {
 namespace {
 
@@ -270,6 +272,105 @@ __global__ void head_rows_kernel(int32_t H, const int32_t* __restrict__ head_ids
   }
 }
 
+// ---- duplicate (document, term) entries of a CSR ------------------------------------
+// The reference keeps a term that one CSR row lists twice as two postings, and its
+// scatter-add sums both into the document's score.  The scorer here updates a list's
+// documents in parallel and needs each document once per list, so the builders merge such
+// entries first: the first occurrence keeps its place in the row, and its weight becomes
+// the fp32 sum of every occurrence's weight, left to right in CSR order.  One warp per row;
+// an entry is compared with every earlier entry of its row (32 at a time), which costs
+// O(nnz^2 / 32) per row: a few milliseconds for millions of SPLADE-sized rows.
+
+// rows [0, n_rows) of indptr (indptr[0] need not be 0): nnz[r] = distinct terms of row r;
+// dropped += entries that repeat an earlier term of their row
+__global__ void dedup_count_kernel(int64_t n_rows, const int64_t* __restrict__ indptr,
+                                   const int32_t* __restrict__ indices, int32_t* __restrict__ nnz,
+                                   unsigned long long* __restrict__ dropped) {
+  const int lane = lane_id();
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  unsigned long long drop = 0;
+  for (int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n_rows; r += warps) {
+    const int64_t e0 = indptr[r], e1 = indptr[r + 1];
+    int32_t kept = 0;
+    for (int64_t j0 = e0; j0 < e1; j0 += 32) {
+      const bool valid = j0 + lane < e1;
+      const int32_t t = valid ? indices[j0 + lane] : 0;
+      bool dup = false;
+      for (int64_t i0 = e0; i0 < j0; i0 += 32) {   // earlier chunks are whole
+        const int32_t u = indices[i0 + lane];
+#pragma unroll 8
+        for (int sl = 0; sl < 32; ++sl) dup |= __shfl_sync(FULL, u, sl) == t;
+      }
+      const uint32_t vmask = __ballot_sync(FULL, valid);
+      const uint32_t peers = __match_any_sync(FULL, valid ? t : int32_t(0x80000000u) + lane) & vmask;
+      dup |= (peers & lanemask_lt()) != 0u;
+      kept += __popc(__ballot_sync(FULL, valid && !dup));
+    }
+    if (lane == 0) {
+      nnz[r] = kept;
+      drop += uint64_t(e1 - e0 - kept);
+    }
+  }
+  if (lane == 0 && drop) atomicAdd(dropped, drop);
+}
+
+// out row r (at new_indptr[r] - new_indptr[0]) = the first occurrence of every term of in
+// row r, in row order, each with the fp32 sum of its occurrences' weights in row order
+// (data and out_data may be null: indices only)
+__global__ void dedup_fill_kernel(int64_t n_rows, const int64_t* __restrict__ indptr,
+                                  const int32_t* __restrict__ indices, const float* __restrict__ data,
+                                  const int64_t* __restrict__ new_indptr, int32_t* __restrict__ out_indices,
+                                  float* __restrict__ out_data) {
+  const int lane = lane_id();
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < n_rows; r += warps) {
+    const int64_t e0 = indptr[r], e1 = indptr[r + 1];
+    int64_t o = new_indptr[r] - new_indptr[0];
+    for (int64_t j0 = e0; j0 < e1; j0 += 32) {
+      const bool valid = j0 + lane < e1;
+      const int32_t t = valid ? indices[j0 + lane] : 0;
+      float w = (valid && data) ? data[j0 + lane] : 0.0f;
+      bool dup = false;
+      for (int64_t i0 = e0; i0 < j0; i0 += 32) {
+        const int32_t u = indices[i0 + lane];
+#pragma unroll 8
+        for (int sl = 0; sl < 32; ++sl) dup |= __shfl_sync(FULL, u, sl) == t;
+      }
+      const uint32_t vmask = __ballot_sync(FULL, valid);
+      const int32_t tk = valid ? t : int32_t(0x80000000u) + lane;
+      const uint32_t peers = __match_any_sync(FULL, tk) & vmask;
+      dup |= (peers & lanemask_lt()) != 0u;
+      const bool first = valid && !dup;
+      if (data) {
+        // later occurrences in this chunk, then in the chunks after it, in row order
+        const float dv = valid ? data[j0 + lane] : 0.0f;
+        for (int sl = 0; sl < 32; ++sl) {
+          const float x = __shfl_sync(FULL, dv, sl);
+          if (first && sl > lane && ((peers >> sl) & 1u)) w = __fadd_rn(w, x);
+        }
+        for (int64_t i0 = j0 + 32; i0 < e1; i0 += 32) {
+          const bool iv = i0 + lane < e1;
+          const int32_t u = iv ? indices[i0 + lane] : 0;
+          const float x = iv ? data[i0 + lane] : 0.0f;
+          const uint32_t um = __ballot_sync(FULL, iv);
+          for (int sl = 0; sl < 32; ++sl) {
+            const int32_t us = __shfl_sync(FULL, u, sl);
+            const float xs = __shfl_sync(FULL, x, sl);
+            if (first && ((um >> sl) & 1u) && us == t) w = __fadd_rn(w, xs);
+          }
+        }
+      }
+      const uint32_t fm = __ballot_sync(FULL, first);
+      if (first) {
+        const int64_t pos = o + __popc(fm & lanemask_lt());
+        out_indices[pos] = t;
+        if (out_data) out_data[pos] = w;
+      }
+      o += __popc(fm);
+    }
+  }
+}
+
 int64_t n_blocks_of(int64_t n_docs, int32_t block_docs) {
   return (n_docs + block_docs - 1) / block_docs;
 }
@@ -283,6 +384,8 @@ using namespace gsp;
 // counts are accumulated in block_starts itself and scanned in place.
 constexpr int64_t kWsCounters = 64;
 constexpr int64_t kWsScan = 256;
+// gsp_check_sorted / gsp_chunk_bounds: two uint64 counters
+constexpr int64_t kCheckWsBytes = 16;
 
 extern "C" int64_t gsp_index_ws_bytes(int64_t n_docs, int32_t V, int32_t block_docs) {
   if (n_docs < 0 || V <= 0 || block_docs <= 0) return -1;
@@ -421,10 +524,11 @@ extern "C" int gsp_index_fill_finish(int64_t n_docs, int32_t V, const int64_t* o
               "filled exactly once with the same CSR rows",
               h[0]);
   // a term listed twice in one document row would give one list a repeated doc id; the
-  // scorer applies a list's postings to distinct documents in parallel, so that is refused
+  // scorer applies a list's postings to distinct documents in parallel, so the builders
+  // merge such entries first (gsp_csr_dedup_*) and a repeat here means they were skipped
   GSP_REQUIRE(h[1] == 0, GSP_ERR_UNSORTED,
               "index build: %llu terms occur twice in one document row (duplicate (doc, term) "
-              "entries); merge them first, e.g. scipy's csr_matrix.sum_duplicates()", h[1]);
+              "entries); merge them first (gsp_csr_dedup_count / gsp_csr_dedup_fill)", h[1]);
   return GSP_OK;
 }
 
@@ -452,6 +556,40 @@ extern "C" int gsp_index_fill(int64_t n_docs, int32_t V, int32_t block_docs, con
                                ws_bytes, stream);
 }
 
+extern "C" int gsp_csr_dedup_count(int64_t n_rows, const int64_t* indptr, const int32_t* indices,
+                                   int32_t* nnz, int64_t* n_dropped, void* ws, int64_t ws_bytes,
+                                   void* stream) {
+  GSP_REQUIRE(n_rows >= 0 && indptr && nnz && n_dropped && ws && ws_bytes >= 8, GSP_ERR_ARG,
+              "gsp_csr_dedup_count: bad arguments");
+  cudaStream_t st = as_stream(stream);
+  unsigned long long* d = static_cast<unsigned long long*>(ws);
+  GSP_CUDA(cudaMemsetAsync(d, 0, 8, st));
+  if (n_rows > 0) {
+    const int64_t blocks = std::min<int64_t>((n_rows + 7) / 8, int64_t(num_sms()) * 32);
+    dedup_count_kernel<<<unsigned(blocks), 256, 0, st>>>(n_rows, indptr, indices, nnz, d);
+    GSP_CHECK_LAUNCH();
+  }
+  unsigned long long h = 0;
+  GSP_CUDA(cudaMemcpyAsync(&h, d, 8, cudaMemcpyDeviceToHost, st));
+  GSP_CUDA(cudaStreamSynchronize(st));
+  *n_dropped = int64_t(h);
+  return GSP_OK;
+}
+
+extern "C" int gsp_csr_dedup_fill(int64_t n_rows, const int64_t* indptr, const int32_t* indices,
+                                  const float* data, const int64_t* new_indptr, int32_t* out_indices,
+                                  float* out_data, void* stream) {
+  GSP_REQUIRE(n_rows >= 0 && indptr && new_indptr && (n_rows == 0 || (indices && out_indices)) &&
+                  ((data == nullptr) == (out_data == nullptr)),
+              GSP_ERR_ARG, "gsp_csr_dedup_fill: bad arguments");
+  if (n_rows == 0) return GSP_OK;
+  const int64_t blocks = std::min<int64_t>((n_rows + 7) / 8, int64_t(num_sms()) * 32);
+  dedup_fill_kernel<<<unsigned(blocks), 256, 0, as_stream(stream)>>>(n_rows, indptr, indices, data, new_indptr,
+                                                                     out_indices, out_data);
+  GSP_CHECK_LAUNCH();
+  return GSP_OK;
+}
+
 extern "C" int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t* offsets,
                                   const int32_t* padded, const float* max_scores,
                                   const float* weights, int32_t wdtype, void* out_weights,
@@ -466,19 +604,19 @@ extern "C" int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t
 }
 
 extern "C" int gsp_check_sorted(int32_t V, const int32_t* doc_ids, const int64_t* offsets,
-                                const int32_t* lengths, int64_t* n_bad, int64_t* n_dup, void* stream) {
-  GSP_REQUIRE(V > 0 && doc_ids && offsets && lengths && n_bad, GSP_ERR_ARG,
-              "gsp_check_sorted: bad arguments");
+                                const int32_t* lengths, int64_t* n_bad, int64_t* n_dup, void* ws,
+                                int64_t ws_bytes, void* stream) {
+  GSP_REQUIRE(V > 0 && doc_ids && offsets && lengths && n_bad && ws && ws_bytes >= kCheckWsBytes,
+              GSP_ERR_ARG, "gsp_check_sorted: bad arguments (workspace needs %lld bytes)",
+              (long long)kCheckWsBytes);
   cudaStream_t st = as_stream(stream);
-  unsigned long long* d_bad = nullptr;
-  GSP_CUDA(cudaMallocAsync(&d_bad, 2 * sizeof(unsigned long long), st));
+  unsigned long long* d_bad = static_cast<unsigned long long*>(ws);
   GSP_CUDA(cudaMemsetAsync(d_bad, 0, 2 * sizeof(unsigned long long), st));
   check_sorted_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, st>>>(V, doc_ids, offsets,
                                                                                  lengths, d_bad);
   GSP_CHECK_LAUNCH();
   unsigned long long h[2] = {0, 0};
   GSP_CUDA(cudaMemcpyAsync(h, d_bad, sizeof(h), cudaMemcpyDeviceToHost, st));
-  GSP_CUDA(cudaFreeAsync(d_bad, st));
   GSP_CUDA(cudaStreamSynchronize(st));
   *n_bad = int64_t(h[0]);
   if (n_dup) *n_dup = int64_t(h[1]);
@@ -486,12 +624,12 @@ extern "C" int gsp_check_sorted(int32_t V, const int32_t* doc_ids, const int64_t
 }
 
 extern "C" int gsp_chunk_bounds(int64_t n_docs, int32_t V, int64_t doc_chunk, const int32_t* doc_ids,
-                                const int64_t* offsets, const int32_t* lengths, int64_t* out,
-                                void* stream) {
+                                const int64_t* offsets, const int32_t* lengths, int64_t* out, void* ws,
+                                int64_t ws_bytes, void* stream) {
   GSP_REQUIRE(n_docs >= 0 && V > 0 && doc_chunk > 0 && out, GSP_ERR_ARG,
               "gsp_chunk_bounds: bad arguments");
   int64_t n_bad = 0;
-  int rc = gsp_check_sorted(V, doc_ids, offsets, lengths, &n_bad, nullptr, stream);
+  int rc = gsp_check_sorted(V, doc_ids, offsets, lengths, &n_bad, nullptr, ws, ws_bytes, stream);
   if (rc) return rc;
   GSP_REQUIRE(n_bad == 0, GSP_ERR_UNSORTED,
               "%lld posting lists are not ascending in doc_id. Chunked scoring requires "

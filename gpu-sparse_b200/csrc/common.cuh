@@ -44,13 +44,19 @@ int max_smem_optin();
 // for this kernel on the current device before.
 int ensure_smem(const void* func, int bytes);
 
+// Largest k whose keys one CTA sorts in shared memory; above it the selection sorts in
+// global memory and needs a workspace of large_k_ws_bytes(B, k).
+constexpr int kMaxSmemK = 8192;
+int64_t large_k_ws_bytes(int64_t B, int64_t k);
+
 // Exact top-k over packed candidate lists (select.cu); counts either on the device
-// (counts_dev[b * cstride_b + r]) or, for at most 64 lists, on the host.
+// (counts_dev[b * cstride_b + r]) or, for at most 64 lists, on the host.  large_ws:
+// large_k_ws_bytes(B, k) bytes of device scratch, needed only when k > kMaxSmemK.
 int merge_topk_device(const uint64_t* keys, int64_t B, int64_t R, int64_t stride_b,
                       int64_t stride_r, const int32_t* counts_dev, int64_t cstride_b,
                       const int32_t* counts_host, int64_t k, float* out_scores, int64_t* out_ids,
                       uint64_t* out_keys, cudaStream_t st, int64_t pad_id = -1,
-                      const int32_t* fault = nullptr);
+                      const int32_t* fault = nullptr, void* large_ws = nullptr);
 // Lists per node of the small-batch merge tree.
 #ifndef GSP_TREE_FAN_IN
 #define GSP_TREE_FAN_IN 8

@@ -50,7 +50,7 @@
 //     larger is better, ties go to the lower doc id) and the keys whose score reaches the
 //     query's threshold go to its candidate buffer.  A discarded key is beaten by k kept
 //     keys, so the final top-k (merge_kernel in select.cu) is exact.  In the small-batch
-//     mode (kTree) the tile instead writes its own exact top-k' to a list of its own, and
+//     mode (kModeTree) the tile instead writes its own exact top-k' to a list of its own, and
 //     a merge tree reduces the lists (no shared buffers, atomics or waits).
 // Each cell therefore accumulates acc = fma(q_w, d_w, acc) in a fixed order -- head terms
 // by term id, then tail terms by term id, a repeated term in query-slot order -- with one
@@ -74,7 +74,7 @@ constexpr int kWarps = 8;
 #endif
 constexpr int kCtasPerSm = GSP_SCORE_CTAS_PER_SM;
 constexpr int kPlanThreads = 256;
-constexpr int kMaxWidth = 4096;   // query slots (W) supported
+constexpr int kMaxWidth = 16384;  // query slots (W) supported: the plan sorts them in shared memory
 constexpr int kBlock = 1024;      // documents per index block (block_starts row)
 #ifndef GSP_TILE_BLOCKS
 #define GSP_TILE_BLOCKS 1         // index blocks per scoring tile
@@ -94,6 +94,7 @@ constexpr int kCompactUnroll = 8;     // keys per lane loaded together by a comp
 constexpr int kMaxPeers = 8;          // other shards' threshold boards one launch raises
 constexpr int kTreeMinK = 256;        // small-batch mode: smallest k' and most query-tiles
 constexpr int64_t kTreeMaxTiles = 24576;
+constexpr int64_t kDenseBytes = int64_t(2) << 30;   // dense mode: keys of one query window
 
 struct ScoreParams {
   const int32_t* doc_ids;
@@ -146,7 +147,20 @@ struct ScoreParams {
   // merges reduces them (no atomics, no waits).
   uint64_t* tile_out;
   int32_t tile_k;
+  // Queries [q_lo, q_lo + q_n) are this launch's (all B except in the dense mode, which
+  // scores the batch a window of queries at a time).
+  int32_t q_lo, q_n;
+  // Dense mode (k above what the candidate buffers hold): every tile writes the keys of
+  // all its documents to dense [q_n, dense_ld] (0 past the last document).
+  uint64_t* dense;
+  int64_t dense_ld;
 };
+
+// How a launch selects: shared candidate buffers, per-tile lists and a merge tree (small
+// batches), or every key written out (k above kMaxSmemK).
+constexpr int kModeBuffers = 0;
+constexpr int kModeTree = 1;
+constexpr int kModeDense = 2;
 
 namespace {
 
@@ -788,8 +802,9 @@ __global__ void final_counts_kernel(int32_t B, int32_t k, const unsigned long lo
 }
 
 // WT: posting weight type; HT: head row type (WT, or float rows for uint8 postings);
-// kTree: small-batch mode (per-tile top-k lists instead of the shared candidate buffers).
-template <typename WT, typename HT, bool kTree>
+// kMode: kModeBuffers, kModeTree (per-tile top-k lists instead of the shared candidate
+// buffers) or kModeDense (every key written out).
+template <typename WT, typename HT, int kMode>
 __global__ void __launch_bounds__(kWarps * 32, kCtasPerSm)
 score_kernel(const ScoreParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -800,7 +815,7 @@ score_kernel(const ScoreParams p) {
   const WT* __restrict__ wts = static_cast<const WT*>(p.weights);
   const HT* __restrict__ hrows = static_cast<const HT*>(p.head_rows);
   const int32_t* __restrict__ doc_ids = p.doc_ids;
-  const unsigned long long n_items = (unsigned long long)p.B * unsigned(p.n_blocks);
+  const unsigned long long n_items = (unsigned long long)p.q_n * unsigned(p.n_blocks);
   unsigned long long nit = 0;   // the claimed item (lane 0)
   if (lane == 0) nit = atomicAdd(p.item_next, 1ull);
   for (;;) {
@@ -810,8 +825,8 @@ score_kernel(const ScoreParams p) {
     if (lane == 0) nit = atomicAdd(p.item_next, 1ull);
     // items stay below 2^31 (make_cfg), so 32-bit division suffices
     const uint32_t it32 = uint32_t(it);
-    const int32_t b = int32_t(it32 / uint32_t(p.B));
-    const int32_t q = int32_t(it32 - uint32_t(b) * uint32_t(p.B));
+    const int32_t b = int32_t(it32 / uint32_t(p.q_n));
+    const int32_t q = p.q_lo + int32_t(it32 - uint32_t(b) * uint32_t(p.q_n));
     const int64_t pbase = int64_t(q) * p.ecap;
     const int32_t nhe = p.n_head_e[q];
     const int32_t nr = p.n_runs[q];
@@ -979,10 +994,28 @@ score_kernel(const ScoreParams p) {
         for (int o = 16; o; o >>= 1) bnd = min(bnd, __shfl_xor_sync(FULL, bnd, o));
         thr = max(thr, uint64_t(bnd));
       }
-      if constexpr (kTree) {
+      if constexpr (kMode == kModeTree) {
         // small-batch mode (one selection pass per tile): the tile's own exact top-k
         tile_topk(acc, span, uint32_t(p.doc_base + d0i), min(p.tile_k, int32_t(span)), p.tile_k, hist,
                   p.tile_out + (int64_t(q) * p.n_blocks + b) * p.tile_k);
+        continue;
+      }
+      if constexpr (kMode == kModeDense) {
+        // every document's key (lane writes columns 128 i + 4 lane .. + 3, two 16-byte stores)
+        uint64_t* __restrict__ row = p.dense + int64_t(q - p.q_lo) * p.dense_ld + d0i;
+        const uint32_t dbase = uint32_t(p.doc_base + d0i);
+#pragma unroll
+        for (int i = 0; i < kTile / 128; ++i) {
+          const uint32_t c = uint32_t(128 * i + 4 * lane);
+          const float4 v = *reinterpret_cast<const float4*>(acc + c);
+          ulonglong2 k0, k1;
+          k0.x = c + 0 < span ? pack_key(v.x, dbase + c + 0) : 0ull;
+          k0.y = c + 1 < span ? pack_key(v.y, dbase + c + 1) : 0ull;
+          k1.x = c + 2 < span ? pack_key(v.z, dbase + c + 2) : 0ull;
+          k1.y = c + 3 < span ? pack_key(v.w, dbase + c + 3) : 0ull;
+          *reinterpret_cast<ulonglong2*>(row + c) = k0;
+          *reinterpret_cast<ulonglong2*>(row + c + 2) = k1;
+        }
         continue;
       }
 #pragma unroll
@@ -1013,6 +1046,8 @@ score_kernel(const ScoreParams p) {
 
 struct Cfg {
   bool tree = false;   // small-batch mode: per-tile top-k lists and a merge tree
+  bool dense = false;  // k above kMaxSmemK: all keys written, a window of queries at a time
+  int64_t dense_q = 0, dense_ld = 0, off_dense = 0, off_large = 0;
   int64_t off_tiles = 0, off_lv0 = 0, off_lv1 = 0;
   int npow2 = 0, cap = 0, smem = 0, ctas_per_sm = 0, grid = 0;
   int64_t ecap = 0, n_blocks = 0, n_iblocks = 0, kk = 0, stride = 0;
@@ -1042,7 +1077,7 @@ void set_layout(Cfg& c, int64_t B) {
   c.off_rend = o; o = align256(o + E * 2);
   c.off_rw0 = o; o = align256(o + E * 4);
   c.off_entw = o; o = align256(o + E * 4);
-  c.off_cand = o; o = align256(o + B * 3 * c.stride * 8);
+  c.off_cand = o; o = align256(o + (c.dense ? 0 : B * 3 * c.stride * 8));
   c.off_counts = o; o = align256(o + B * 3 * 4);
   // cleared by every call: thresholds [B] u64, reservation words [B] u64, written
   // counters [B, 2], finished compactions [B], item counter u64, fault flag
@@ -1052,6 +1087,10 @@ void set_layout(Cfg& c, int64_t B) {
     c.off_tiles = o; o = align256(o + B * c.n_blocks * c.kk * 8);
     c.off_lv0 = o; o = align256(o + B * g1 * c.kk * 8);
     c.off_lv1 = o; o = align256(o + B * ((g1 + kTreeFanIn - 1) / kTreeFanIn) * c.kk * 8);
+  }
+  if (c.dense) {
+    c.off_dense = o; o = align256(o + c.dense_q * c.dense_ld * 8);
+    c.off_large = o; o = align256(o + large_k_ws_bytes(c.dense_q, c.kk));
   }
   c.total = o;
 }
@@ -1069,8 +1108,7 @@ int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) 
   GSP_REQUIRE(ix->n_head >= 0 && ix->n_head <= 65535 && (ix->n_head == 0 || (ix->head_slot && ix->head_rows)),
               GSP_ERR_ARG, "score: bad head rows");
   c.kk = std::min<int64_t>(k, ix->n_docs);
-  GSP_REQUIRE(c.kk <= 8192, GSP_ERR_UNSUPPORTED, "score: top_k %lld exceeds the supported maximum 8192",
-              (long long)c.kk);
+  GSP_REQUIRE(c.kk < 0x7FFFFFFFll, GSP_ERR_UNSUPPORTED, "score: top_k %lld too large", (long long)c.kk);
   const int sms = num_sms();
   c.ecap = W;
   c.smem = WarpLayout::total * kWarps;
@@ -1094,6 +1132,17 @@ int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) 
   // compactions are short anyway.
   c.tree = kTile == kSel && c.kk <= kSel && c.kk >= kTreeMinK && c.n_blocks > 0 && B > 0 &&
            B * c.n_blocks <= kTreeMaxTiles && B * c.n_blocks * c.kk * 8 <= g_tree_limit.load();
+  // Above kMaxSmemK keys per query the candidate buffers and the shared-memory sort do not
+  // apply: every key is written out for a window of queries whose keys (and the global
+  // sort's two buffers) fit about kDenseBytes, and the windows are selected one by one.
+  c.dense = c.kk > kMaxSmemK;
+  if (c.dense) {
+    c.dense_ld = c.n_blocks * kTile;
+    const int64_t per_q = c.dense_ld * 8 + large_k_ws_bytes(1, c.kk);
+    c.dense_q = std::max<int64_t>(1, std::min<int64_t>(B, kDenseBytes / per_q));
+    GSP_REQUIRE(c.dense_q * c.n_blocks < (int64_t(1) << 31), GSP_ERR_UNSUPPORTED,
+                "score: too many documents for the dense selection");
+  }
   set_layout(c, B);
   return GSP_OK;
 }
@@ -1113,7 +1162,8 @@ Profile& profile() {
 
 template <typename WT, typename HT>
 int launch_score(const ScoreParams& p, const Cfg& c, cudaStream_t st) {
-  auto kern = c.tree ? score_kernel<WT, HT, true> : score_kernel<WT, HT, false>;
+  auto kern = c.dense ? score_kernel<WT, HT, kModeDense>
+                      : (c.tree ? score_kernel<WT, HT, kModeTree> : score_kernel<WT, HT, kModeBuffers>);
   if (int rc = ensure_smem(reinterpret_cast<const void*>(kern), c.smem)) return rc;
   Profile& pr = profile();
   std::pair<cudaEvent_t, cudaEvent_t>* evp = nullptr;
@@ -1212,6 +1262,10 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.kg = n_shards > 1 ? int32_t((c.kk + n_shards - 1) / n_shards) : 0;
   p.tile_out = c.tree ? reinterpret_cast<uint64_t*>(w + c.off_tiles) : nullptr;
   p.tile_k = int32_t(c.kk);
+  p.q_lo = 0;
+  p.q_n = int32_t(B);
+  p.dense = c.dense ? reinterpret_cast<uint64_t*>(w + c.off_dense) : nullptr;
+  p.dense_ld = c.dense_ld;
   for (int r = 0; r < kMaxPeers; ++r) {
     p.peer_thr[r] = r < p.n_peers ? reinterpret_cast<unsigned long long*>(peers[r]) : nullptr;
     GSP_REQUIRE(r >= p.n_peers || p.peer_thr[r], GSP_ERR_ARG, "gsp_score_topk_shared: null peer board %d", r);
@@ -1226,20 +1280,40 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
       ix->wdtype == GSP_W_U8 ? ix->term_scale : nullptr, p);
   GSP_CHECK_LAUNCH();
 
-  if (c.n_blocks > 0) {
-    // head rows share the postings' type, except that uint8 postings may have fp32 rows
-    const int32_t hdt = ix->n_head > 0 ? ix->head_wdtype : ix->wdtype;
-    GSP_REQUIRE(hdt == ix->wdtype || (ix->wdtype == GSP_W_U8 && hdt == GSP_W_F32), GSP_ERR_ARG,
-                "gsp_score_topk: head rows of type %d do not go with weights of type %d", hdt,
-                ix->wdtype);
+  // head rows share the postings' type, except that uint8 postings may have fp32 rows
+  const int32_t hdt = ix->n_head > 0 ? ix->head_wdtype : ix->wdtype;
+  GSP_REQUIRE(hdt == ix->wdtype || (ix->wdtype == GSP_W_U8 && hdt == GSP_W_F32), GSP_ERR_ARG,
+              "gsp_score_topk: head rows of type %d do not go with weights of type %d", hdt, ix->wdtype);
+  auto launch = [&](const ScoreParams& pp) -> int {
     switch (ix->wdtype) {
-      case GSP_W_F32: rc = launch_score<float, float>(p, c, st); break;
-      case GSP_W_BF16: rc = launch_score<__nv_bfloat16, __nv_bfloat16>(p, c, st); break;
+      case GSP_W_F32: return launch_score<float, float>(pp, c, st);
+      case GSP_W_BF16: return launch_score<__nv_bfloat16, __nv_bfloat16>(pp, c, st);
       case GSP_W_U8:
-        rc = hdt == GSP_W_F32 ? launch_score<uint8_t, float>(p, c, st) : launch_score<uint8_t, uint8_t>(p, c, st);
-        break;
+        return hdt == GSP_W_F32 ? launch_score<uint8_t, float>(pp, c, st) : launch_score<uint8_t, uint8_t>(pp, c, st);
       default: set_error("gsp_score_topk: unknown weight dtype %d", ix->wdtype); return GSP_ERR_ARG;
     }
+  };
+  if (c.dense) {
+    // a window of dense_q queries at a time: all their keys, then the exact top-k' of each
+    // row (radix select over the row, global sort of the k' keys)
+    for (int64_t q0 = 0; q0 < B; q0 += c.dense_q) {
+      const int64_t qn = std::min<int64_t>(c.dense_q, B - q0);
+      ScoreParams pw = p;
+      pw.q_lo = int32_t(q0);
+      pw.q_n = int32_t(qn);
+      GSP_CUDA(cudaMemsetAsync(p.item_next, 0, sizeof(unsigned long long), st));
+      rc = launch(pw);
+      if (rc) return rc;
+      const int32_t row_len = int32_t(c.dense_ld);
+      rc = merge_topk_device(pw.dense, qn, 1, c.dense_ld, c.dense_ld, nullptr, 0, &row_len, c.kk,
+                             out_scores + q0 * c.kk, out_ids + q0 * c.kk, out_keys ? out_keys + q0 * c.kk : nullptr,
+                             st, -1, p.fault, w + c.off_large);
+      if (rc) return rc;
+    }
+    return GSP_OK;
+  }
+  if (c.n_blocks > 0) {
+    rc = launch(p);
     if (rc) return rc;
   }
   if (c.tree) {
@@ -1353,13 +1427,21 @@ void* g_noalloc_ptr[256] = {nullptr};   // device address of the array, per devi
 }  // namespace
 
 // Host code may not use g_noalloc_scratch as an address (it is a host-side stand-in), so
-// the device address is looked up once per device, with that device current.
-static int noalloc_scratch(void** out) {
+// the device address is looked up with the device current.  It is looked up again on every
+// call whose stream is not being captured (the address belongs to the current context, so
+// a device reset or another driver-API context gets its own), and remembered per device for
+// calls made during a stream capture, which reuse the address of the last call outside one.
+static int noalloc_scratch(void** out, cudaStream_t st) {
   int dev = 0;
   GSP_CUDA(cudaGetDevice(&dev));
   GSP_REQUIRE(dev >= 0 && dev < 256, GSP_ERR_UNSUPPORTED, "noalloc: device ordinal %d out of range", dev);
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
+    (void)cudaGetLastError();
+    cs = cudaStreamCaptureStatusActive;   // cannot tell: treat it as a capture
+  }
   std::lock_guard<std::mutex> g(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  if (cs == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p) {
@@ -1368,6 +1450,8 @@ static int noalloc_scratch(void** out) {
     }
     g_noalloc_ptr[dev] = p;
   }
+  GSP_REQUIRE(g_noalloc_ptr[dev], GSP_ERR_UNSUPPORTED,
+              "gsp_score_topk_noalloc: the first call on a device must come before any stream capture");
   *out = g_noalloc_ptr[dev];
   return GSP_OK;
 }
@@ -1378,11 +1462,13 @@ extern "C" int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* q
   Cfg c;
   int rc = make_cfg(ix, B, W, k, c);
   if (rc) return rc;
-  // fewer streams shrink the candidate buffers; the result does not depend on the stream
-  // count, only the parallelism does
   // a smaller candidate capacity means more frequent compactions, never another result;
-  // the smallest one keeps k keys plus a whole tile
+  // the smallest one keeps k keys plus a whole tile.  The default capacity is already that
+  // minimum up to k' = 2048, so only larger k' can shrink.
   const int min_cap = int(((c.kk + kSel + 31) / 32) * 32);
+  GSP_REQUIRE(!c.dense, GSP_ERR_UNSUPPORTED,
+              "gsp_score_topk_noalloc: top_k %lld is above %d; use gsp_score_topk with a workspace",
+              (long long)c.kk, kMaxSmemK);
   if (c.tree) {   // the per-tile lists would not fit the fixed scratch: shared buffers only
     c.tree = false;
     set_layout(c, B);
@@ -1396,7 +1482,7 @@ extern "C" int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* q
               "fixed %lld (lower the batch size or top_k, or use gsp_score_topk with a workspace)",
               (long long)c.total, (long long)kNoAllocScratchBytes);
   void* scratch = nullptr;
-  rc = noalloc_scratch(&scratch);
+  rc = noalloc_scratch(&scratch, as_stream(stream));
   if (rc) return rc;
   // Every buffer in the scratch is written before it is read within a call except the
   // per-query thresholds and buffer counters, the item counter and the fault flag, which

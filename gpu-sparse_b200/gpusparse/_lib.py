@@ -25,16 +25,17 @@ GSP_ERR_UNSUPPORTED = 6
 GSP_ERR_BLOCK_PL = 7
 
 W_F32, W_BF16, W_U8 = 0, 1, 2
+CHECK_WS_BYTES = 16     # GSP_CHECK_WS_BYTES
 
 # every symbol include/gpusparse.h declares
 EXPORTS = (
     "gsp_last_error", "gsp_version", "gsp_scan_i32", "gsp_scan_ws_bytes", "gsp_synth_nnz",
     "gsp_synth_fill", "gsp_index_ws_bytes", "gsp_index_count", "gsp_index_fill",
     "gsp_index_count_chunk", "gsp_index_count_finish", "gsp_index_fill_chunk",
-    "gsp_index_fill_finish",
+    "gsp_index_fill_finish", "gsp_csr_dedup_count", "gsp_csr_dedup_fill",
     "gsp_index_quantize", "gsp_index_head_rows", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
     "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_score_topk_shared", "gsp_board_alloc",
-    "gsp_board_free", "gsp_board_open", "gsp_board_close", "gsp_board_clear", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_set_tree_limit", "gsp_get_tree_limit", "gsp_merge_topk",
+    "gsp_board_free", "gsp_board_open", "gsp_board_close", "gsp_board_clear", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_set_tree_limit", "gsp_get_tree_limit", "gsp_merge_ws_bytes", "gsp_merge_topk",
     "gsp_compacted_ws_bytes", "gsp_compacted_topk",
 )
 
@@ -93,11 +94,13 @@ def lib() -> ctypes.CDLL:
             "gsp_index_fill_chunk": (ctypes.c_int, [i64, i32, i32, i64, i64, p, p, p, p, p, p, p,
                                                     p, i64, p]),
             "gsp_index_fill_finish": (ctypes.c_int, [i64, i32, p, p, p, p, p, p, i64, p]),
+            "gsp_csr_dedup_count": (ctypes.c_int, [i64, p, p, p, ctypes.POINTER(i64), p, i64, p]),
+            "gsp_csr_dedup_fill": (ctypes.c_int, [i64, p, p, p, p, p, p, p]),
             "gsp_index_quantize": (ctypes.c_int, [i32, i64, p, p, p, p, i32, p, p, p]),
             "gsp_index_head_rows": (ctypes.c_int, [i32, p, p, p, p, p, i32, i64, p, p]),
             "gsp_check_sorted": (ctypes.c_int, [i32, p, p, p, ctypes.POINTER(i64),
-                                                ctypes.POINTER(i64), p]),
-            "gsp_chunk_bounds": (ctypes.c_int, [i64, i32, i64, p, p, p, p, p]),
+                                                ctypes.POINTER(i64), p, i64, p]),
+            "gsp_chunk_bounds": (ctypes.c_int, [i64, i32, i64, p, p, p, p, p, i64, p]),
             "gsp_score_ws_bytes": (i64, [ctypes.POINTER(IndexView), i64, i64, i64]),
             "gsp_score_topk": (ctypes.c_int, [ctypes.POINTER(IndexView), p, p, i64, i64, i64, p,
                                               p, p, p, i64, p]),
@@ -117,7 +120,8 @@ def lib() -> ctypes.CDLL:
             "gsp_get_tree_limit": (i64, []),
             "gsp_profile_collect": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double),
                                                    ctypes.POINTER(i64)]),
-            "gsp_merge_topk": (ctypes.c_int, [p, i64, i64, i64, i64, p, i64, p, p, p, p]),
+            "gsp_merge_ws_bytes": (i64, [i64, i64]),
+            "gsp_merge_topk": (ctypes.c_int, [p, i64, i64, i64, i64, p, i64, p, p, p, p, i64, p]),
             "gsp_compacted_ws_bytes": (i64, [i64, i64, i64, i64]),
             "gsp_compacted_topk": (ctypes.c_int, [p, i64, i64, i64, p, i64, i64, p, p, p, i64,
                                                   p]),

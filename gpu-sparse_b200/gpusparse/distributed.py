@@ -94,7 +94,8 @@ class ThresholdBoards:
     (the all-to-all of candidate keys), which no rank finishes before every rank's scoring
     kernel of that batch has ended.
     Raises of the current batch that land before the clear are lost, which only weakens a
-    bound.  If a peer's board cannot be mapped, this rank raises only its own board."""
+    bound.  If a peer's board cannot be mapped, this rank scores without any board: it
+    neither reads a bound nor publishes one, so its row stays 0 (no bound) everywhere."""
 
     def __init__(self, device: torch.device, capacity: int, group=None):
         """capacity: queries per batch the boards hold (G rows of capacity keys each)."""

@@ -123,7 +123,9 @@ def build_streamed(num_docs: int, vocab_size: int, get_chunk, device,
             if dt.numel() != ix.numel():
                 raise ValueError(f"chunk [{lo}, {hi}): {ix.numel()} indices but {dt.numel()} "
                                  "weights")
-        return ip, ix, dt
+        else:
+            dt = None
+        return merge_duplicates(ip, ix, dt)
 
     with torch.cuda.device(device):
         st = L.stream_of(device)
@@ -167,6 +169,37 @@ def build_streamed(num_docs: int, vocab_size: int, get_chunk, device,
         if block_docs == BLOCK_DOCS:
             ensure_head(idx, head_ids=head_ids)
     return idx
+
+
+def merge_duplicates(indptr: torch.Tensor, indices: torch.Tensor, data=None):
+    """Device CSR rows with every term once: a term that a row lists more than once keeps
+    its first position and the fp32 sum of its weights in row order (the reference keeps
+    both entries as postings and its scatter-add sums them per document).  Returns the
+    inputs unchanged when no row repeats a term; ``indptr`` may start above 0."""
+    n = indptr.numel() - 1
+    dev = indptr.device
+    lib = L.lib()
+    if n <= 0 or indices.numel() == 0:
+        return indptr, indices, data
+    nnz = torch.empty(n, dtype=torch.int32, device=dev)
+    dropped = ctypes.c_int64(0)
+    ws = L.workspace(8, dev)
+    st = L.stream_of(dev)
+    L.check(lib.gsp_csr_dedup_count(n, L.ptr(indptr), L.ptr(indices), L.ptr(nnz),
+                                    ctypes.byref(dropped), L.ptr(ws), ws.numel(), st),
+            "merge duplicate entries")
+    if dropped.value == 0:
+        return indptr, indices, data
+    new_ip = torch.empty(n + 1, dtype=torch.int64, device=dev)
+    sws = L.workspace(lib.gsp_scan_ws_bytes(n), dev)
+    L.check(lib.gsp_scan_i32(L.ptr(nnz), n, L.ptr(new_ip), L.ptr(sws), sws.numel(), st),
+            "merge duplicate entries")
+    total = int(indptr[-1].item() - indptr[0].item()) - int(dropped.value)
+    out_ix = torch.empty(total, dtype=torch.int32, device=dev)
+    out_dt = torch.empty(total, dtype=torch.float32, device=dev) if data is not None else None
+    L.check(lib.gsp_csr_dedup_fill(n, L.ptr(indptr), L.ptr(indices), L.ptr(data), L.ptr(new_ip),
+                                   L.ptr(out_ix), L.ptr(out_dt), st), "merge duplicate entries")
+    return new_ip, out_ix, out_dt
 
 
 def build_from_host_csr(indptr, indices, data, vocab_size: int, device,
@@ -238,9 +271,11 @@ def ensure_blocks(index: GPUInvertedIndex) -> None:
     dev = index.device if isinstance(index.device, torch.device) else torch.device(index.device)
     n_bad, n_dup = ctypes.c_int64(0), ctypes.c_int64(0)
     with torch.cuda.device(dev):
+        ws = L.workspace(L.CHECK_WS_BYTES, dev)
         L.check(L.lib().gsp_check_sorted(int(index.vocab_size), L.ptr(index.doc_ids),
                                          L.ptr(index.offsets), L.ptr(index.lengths),
-                                         ctypes.byref(n_bad), ctypes.byref(n_dup), L.stream_of(dev)),
+                                         ctypes.byref(n_bad), ctypes.byref(n_dup), L.ptr(ws),
+                                         ws.numel(), L.stream_of(dev)),
                 "index check")
     if n_dup.value:
         raise ValueError(f"{n_dup.value} posting lists repeat a doc id (a term listed twice in one "

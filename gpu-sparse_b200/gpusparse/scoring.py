@@ -44,7 +44,27 @@ def _prep_queries(index: GPUInvertedIndex, qi: torch.Tensor, qs: torch.Tensor):
         qi = torch.where((qi < 0) | (qi >= V), torch.full_like(qi, -1), qi).to(torch.int32)
     if qs.dtype != torch.float32:
         qs = qs.to(torch.float32)
+    if qi.shape[1] > MAX_WIDTH:
+        qi, qs = _compact_queries(qi, qs, int(index.vocab_size))
     return qi.contiguous(), qs.contiguous()
+
+
+MAX_WIDTH = 16384   # query slots one plan sorts (kMaxWidth in csrc/score.cu)
+
+
+def _compact_queries(qi: torch.Tensor, qs: torch.Tensor, V: int):
+    """Moves every query's scored entries (term id in [0, V)) to the front, keeping their
+    slot order, so that a batch padded wider than MAX_WIDTH needs only its longest query's
+    width; the canonical order (term id, then slot) and so the result are unchanged."""
+    valid = (qi >= 0) & (qi < V)
+    width = int(valid.sum(dim=1).max().item()) if qi.shape[0] else 1
+    if width > MAX_WIDTH:
+        raise RuntimeError(f"a query has {width} scored terms; at most {MAX_WIDTH} are supported")
+    order = torch.sort((~valid).to(torch.int8), dim=1, stable=True).indices[:, :max(width, 1)]
+    keep = torch.gather(valid, 1, order)
+    qi = torch.where(keep, torch.gather(qi, 1, order), torch.full_like(order, -1, dtype=qi.dtype))
+    qs = torch.where(keep, torch.gather(qs, 1, order), torch.zeros_like(order, dtype=qs.dtype))
+    return qi.to(torch.int32), qs
 
 
 def score_topk(index: GPUInvertedIndex, query_term_ids: torch.Tensor,
@@ -129,9 +149,11 @@ def build_chunk_boundaries(index, doc_chunk: int) -> torch.Tensor:
     n_chunks = (N + doc_chunk - 1) // doc_chunk
     out = torch.empty((n_chunks + 1, V), dtype=torch.int64, device=dev)
     with torch.cuda.device(dev):
+        ws = L.workspace(L.CHECK_WS_BYTES, dev)
         L.check(L.lib().gsp_chunk_bounds(N, V, int(doc_chunk), L.ptr(index.doc_ids),
                                          L.ptr(index.offsets), L.ptr(index.lengths), L.ptr(out),
-                                         L.stream_of(dev)), "build_chunk_boundaries")
+                                         L.ptr(ws), ws.numel(), L.stream_of(dev)),
+                "build_chunk_boundaries")
     return out
 
 
@@ -208,9 +230,14 @@ def merge_topk(keys: torch.Tensor, counts, k: int, stride_r: Optional[int] = Non
     k = int(k)
     s = torch.empty((B, k), dtype=torch.float32, device=dev)
     i = torch.empty((B, k), dtype=torch.int64, device=dev)
+    lib = L.lib()
     with torch.cuda.device(dev):
-        L.check(L.lib().gsp_merge_topk(L.ptr(keys), B, R, kin, B * kin, cnt, k, L.ptr(s),
-                                       L.ptr(i), None, L.stream_of(dev)), "merge_topk")
+        nb = lib.gsp_merge_ws_bytes(B, k)
+        if nb < 0:
+            L.check(int(-nb), "merge_topk")
+        ws = L.workspace(nb, dev) if nb > 0 else None
+        L.check(lib.gsp_merge_topk(L.ptr(keys), B, R, kin, B * kin, cnt, k, L.ptr(s), L.ptr(i),
+                                   None, L.ptr(ws), int(nb), L.stream_of(dev)), "merge_topk")
     return s, i
 
 

@@ -30,7 +30,6 @@ from triton_kernel import triton_fused_score  # noqa: E402
 from triton_kernel_chunked import build_chunk_boundaries  # noqa: E402
 from fused_topk import triton_chunked_score_fused  # noqa: E402
 
-BLOCK = 32          # posting lists are padded to a warp boundary
 VOCAB_PAD = 1       # vocabulary is sized from the data, plus one
 
 

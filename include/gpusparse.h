@@ -118,6 +118,22 @@ int gsp_index_fill_chunk(int64_t n_docs, int32_t V, int32_t block_docs, int64_t 
 int gsp_index_fill_finish(int64_t n_docs, int32_t V, const int64_t* offsets,
                           const int32_t* lengths, int32_t* doc_ids, float* weights,
                           float* max_scores, void* ws, int64_t ws_bytes, void* stream);
+/* Duplicate (document, term) entries.  The reference keeps a term that one CSR row lists
+ * twice as two postings and its scatter-add sums both (lsr_benchmark_engine/
+ * gpusparse_retrieval.py:84-105, src/triton_kernel.py:93-156); the scorer here needs each
+ * document once per list, so the builders merge them first: the first occurrence keeps
+ * its place and its weight becomes the fp32 sum of all occurrences' weights in row order.
+ * count: nnz[r] = distinct terms of row r (rows [0, n_rows) of indptr, whose first entry
+ * need not be 0), *n_dropped (host; the call synchronises) = entries merged away;
+ * ws >= 8 bytes of device scratch.  fill: the merged rows at new_indptr (n_rows + 1
+ * entries, e.g. the scan of nnz) relative to new_indptr[0]; data and out_data may both be
+ * NULL to merge the indices only. */
+int gsp_csr_dedup_count(int64_t n_rows, const int64_t* indptr, const int32_t* indices,
+                        int32_t* nnz, int64_t* n_dropped, void* ws, int64_t ws_bytes,
+                        void* stream);
+int gsp_csr_dedup_fill(int64_t n_rows, const int64_t* indptr, const int32_t* indices,
+                       const float* data, const int64_t* new_indptr, int32_t* out_indices,
+                       float* out_data, void* stream);
 /* fp32 weights -> bf16 (round to nearest even) or uint8 impacts with per-term scale
  * max_scores[t] / 255 (q = clamp(rint(w / scale), 0, 255)). */
 int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t* offsets,
@@ -131,20 +147,24 @@ int gsp_index_head_rows(int32_t H, const int32_t* head_ids, const int64_t* offse
                         const int32_t* lengths, const int32_t* doc_ids, const void* weights,
                         int32_t wdtype, int64_t ld, void* rows, void* stream);
 /* Counts posting lists that are not ascending in doc id (*n_bad) and, when n_dup is not
- * NULL, lists that repeat a doc id (*n_dup); both written on the host.  The scorer needs
- * strictly ascending lists: gsp_index_fill refuses a CSR that lists a term twice in one
- * row, and a caller that assembles an index itself checks n_dup == 0.
+ * NULL, lists that repeat a doc id (*n_dup); both written on the host (this call
+ * synchronises the stream).  ws: at least GSP_CHECK_WS_BYTES of device scratch.  The
+ * scorer needs strictly ascending lists (the CSR builders merge a term listed twice in one
+ * row first); a caller that assembles an index itself checks n_dup == 0.
  * Replaces the check in src/triton_kernel_chunked.py:99-108. */
+#define GSP_CHECK_WS_BYTES 16
 int gsp_check_sorted(int32_t V, const int32_t* doc_ids, const int64_t* offsets,
-                     const int32_t* lengths, int64_t* n_bad, int64_t* n_dup, void* stream);
+                     const int32_t* lengths, int64_t* n_bad, int64_t* n_dup, void* ws,
+                     int64_t ws_bytes, void* stream);
 
 /* ---------------------------------------------------------------- chunk bounds */
 /* build_chunk_boundaries: out int64 [n_chunks+1, V], out[c][t] = offsets[t] + number of
  * postings of t with doc id < min(c*doc_chunk, n_docs).  GSP_ERR_UNSORTED if any list
- * is not ascending (the reference raises ValueError). */
+ * is not ascending (the reference raises ValueError).  ws: GSP_CHECK_WS_BYTES of device
+ * scratch for the order check (which synchronises the stream). */
 int gsp_chunk_bounds(int64_t n_docs, int32_t V, int64_t doc_chunk, const int32_t* doc_ids,
-                     const int64_t* offsets, const int32_t* lengths, int64_t* out,
-                     void* stream);
+                     const int64_t* offsets, const int32_t* lengths, int64_t* out, void* ws,
+                     int64_t ws_bytes, void* stream);
 
 /* ---------------------------------------------------------------- scoring */
 typedef struct gsp_index_view {
@@ -189,14 +209,18 @@ int gsp_score_topk(const gsp_index_view* ix, const int32_t* qi, const float* qs,
  * memory on the call path (a serving loop where cudaMalloc would synchronise the device,
  * or a host that gives the library only its input and output buffers).  No counterpart in
  * the reference.  Scratch is a fixed 32 MiB array compiled into the library, placed on
- * every GPU that loads it and held until exit.  The per-query candidate buffers shrink
- * to their minimum (more frequent compactions, same result); a batch that still does not
- * fit (about B * 3 * (2k + 2048) * 8 bytes plus the plan: some 330 queries at k = 1000)
- * is rejected with GSP_ERR_UNSUPPORTED.
- * Results equal gsp_score_topk's.  The first call on each device looks up the array's
- * device address (cudaGetSymbolAddress) with that device current; make that first call
- * before any stream capture.  All calls on a device share the one array: calls that
- * overlap on the GPU (different streams, or threads) race and must be serialised. */
+ * every GPU that loads it and held until exit.  When a batch does not fit with the default
+ * per-query candidate capacity, the capacity shrinks toward its minimum of k' + 1024 keys
+ * (more frequent compactions, same result; the default equals that minimum up to
+ * k' = 2048, so only larger k' shrink); a batch that still does not fit (about
+ * B * 3 * (2k + 2048) * 8 bytes plus the plan: some 330 queries at k = 1000), or with
+ * k' > 8192, is rejected with GSP_ERR_UNSUPPORTED.
+ * Results equal gsp_score_topk's.  Every call whose stream is not being captured looks up
+ * the array's device address (cudaGetSymbolAddress) in the current context; a call during
+ * a stream capture reuses the address of the device's last call outside one, so make the
+ * first call on each device (and the first after a device reset) before any capture.
+ * All calls on a device share the one array: calls that overlap on the GPU (different
+ * streams, or threads) race and must be serialised. */
 int gsp_score_topk_noalloc(const gsp_index_view* ix, const int32_t* qi, const float* qs,
                            int64_t B, int64_t W, int64_t k, float* out_scores, int64_t* out_ids,
                            uint64_t* out_keys, void* stream);
@@ -263,10 +287,14 @@ int gsp_profile_collect(double* total_ms, int64_t* launches);
  * (fkey(score) << 32 | (0xFFFFFFFF - doc id)), list r of query b at
  * keys + b*stride_b + r*stride_r, holding counts[r] valid entries.  Writes k' =
  * min(k, sum(counts)) results per query (scores fp32, ids int64 and, if non-null,
- * keys).  Replaces the host-side shard merge and the running torch.topk merge. */
+ * keys).  ws: gsp_merge_ws_bytes(B, k) bytes of device scratch (0, and ws may be NULL,
+ * for k <= 8192; above that the keys are sorted in global memory).
+ * Replaces the host-side shard merge and the running torch.topk merge. */
+int64_t gsp_merge_ws_bytes(int64_t B, int64_t k);
 int gsp_merge_topk(const uint64_t* keys, int64_t B, int64_t R, int64_t stride_b,
                    int64_t stride_r, const int32_t* counts_host, int64_t k,
-                   float* out_scores, int64_t* out_ids, uint64_t* out_keys, void* stream);
+                   float* out_scores, int64_t* out_ids, uint64_t* out_keys, void* ws,
+                   int64_t ws_bytes, void* stream);
 /* compacted_topk: top-min(k, L) of row entries >= tau[b] of scores [B, L] (row stride
  * `stride` floats), (score desc, column asc), padded with (-inf, 0) when fewer. */
 int64_t gsp_compacted_ws_bytes(int64_t B, int64_t L, int64_t k, int64_t max_cand);

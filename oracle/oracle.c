@@ -362,27 +362,51 @@ int orc_score_full(int64_t N, int32_t V, const int32_t* doc_ids, const float* we
 /* ------------------------------------------------------------------ 4. fp64 dense */
 
 /* S[b, d] = sum over query slots with 0 <= t < V of qs * D[d, t], accumulated in fp64
- * straight from the document CSR (duplicates summed, as Q_dense @ D_dense^T does). */
-int orc_score_dense_f64(int64_t N, int32_t V, const int64_t* indptr, const int32_t* indices,
-                        const float* data, int64_t B, int64_t W, const int32_t* qi,
-                        const float* qs, double* out) {
-    double* qd = (double*)calloc((size_t)V, sizeof(double));
-    if (!qd) return 2;
-    for (int64_t b = 0; b < B; ++b) {
-        for (int64_t s = 0; s < W; ++s) {
-            int32_t t = qi[b * W + s];
-            if (t >= 0 && t < V) qd[t] += (double)qs[b * W + s];
+ * straight from the document CSR (duplicates summed, as Q_dense @ D_dense^T does).
+ * Queries are split over nthreads threads. */
+typedef struct {
+    int64_t N; int32_t V; const int64_t* indptr; const int32_t* indices; const float* data;
+    int64_t W; const int32_t* qi; const float* qs; double* out; int64_t b0, b1;
+} dense_job;
+
+static void* dense_worker(void* arg) {
+    dense_job* j = (dense_job*)arg;
+    double* qd = (double*)calloc((size_t)j->V, sizeof(double));
+    if (!qd) return (void*)1;
+    for (int64_t b = j->b0; b < j->b1; ++b) {
+        for (int64_t s = 0; s < j->W; ++s) {
+            int32_t t = j->qi[b * j->W + s];
+            if (t >= 0 && t < j->V) qd[t] += (double)j->qs[b * j->W + s];
         }
-        for (int64_t d = 0; d < N; ++d) {
+        for (int64_t d = 0; d < j->N; ++d) {
             double acc = 0.0;
-            for (int64_t e = indptr[d]; e < indptr[d + 1]; ++e) acc += qd[indices[e]] * (double)data[e];
-            out[b * N + d] = acc;
+            for (int64_t e = j->indptr[d]; e < j->indptr[d + 1]; ++e)
+                acc += qd[j->indices[e]] * (double)j->data[e];
+            j->out[b * j->N + d] = acc;
         }
-        for (int64_t s = 0; s < W; ++s) {
-            int32_t t = qi[b * W + s];
-            if (t >= 0 && t < V) qd[t] = 0.0;
+        for (int64_t s = 0; s < j->W; ++s) {
+            int32_t t = j->qi[b * j->W + s];
+            if (t >= 0 && t < j->V) qd[t] = 0.0;
         }
     }
     free(qd);
-    return 0;
+    return NULL;
+}
+
+int orc_score_dense_f64(int64_t N, int32_t V, const int64_t* indptr, const int32_t* indices,
+                        const float* data, int64_t B, int64_t W, const int32_t* qi,
+                        const float* qs, double* out, int32_t nthreads) {
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 256) nthreads = 256;
+    if (nthreads > B) nthreads = (int32_t)(B > 0 ? B : 1);
+    pthread_t th[256]; dense_job jobs[256];
+    for (int32_t t = 0; t < nthreads; ++t) {
+        dense_job j = {N, V, indptr, indices, data, W, qi, qs, out, B * t / nthreads,
+                       B * (t + 1) / nthreads};
+        jobs[t] = j;
+        pthread_create(&th[t], NULL, dense_worker, &jobs[t]);
+    }
+    int rc = 0;
+    for (int32_t t = 0; t < nthreads; ++t) { void* r; pthread_join(th[t], &r); if (r) rc = 2; }
+    return rc;
 }

@@ -62,7 +62,7 @@ def lib():
         L.orc_build_fill.argtypes = [i64, i32, p, p, p, p, p, p, p]
         L.orc_score_topk.argtypes = [i64, i32, p, p, p, p, i64, i64, p, p, i64, i64, i32, p, p, p]
         L.orc_score_full.argtypes = [i64, i32, p, p, p, p, i64, i64, p, p, i32, p, p]
-        L.orc_score_dense_f64.argtypes = [i64, i32, p, p, p, i64, i64, p, p, p]
+        L.orc_score_dense_f64.argtypes = [i64, i32, p, p, p, i64, i64, p, p, p, i32]
         for f in ("orc_synth_nnz", "orc_synth_fill", "orc_build_lengths", "orc_build_fill",
                   "orc_score_topk", "orc_score_full", "orc_score_dense_f64"):
             getattr(L, f).restype = ctypes.c_int
@@ -221,6 +221,45 @@ def build_index_reference(csr, vocab_size: int | None = None) -> Index:
                  num_docs, V)
 
 
+def merge_duplicates(indptr: np.ndarray, indices: np.ndarray, data: np.ndarray):
+    """CSR rows with every term once, as the library's builders see them.  The reference
+    keeps a term that one row lists twice as two postings and sums both in its scatter-add
+    (``lsr_benchmark_engine/gpusparse_retrieval.py:84-105`` builds from the raw CSR;
+    ``src/triton_kernel.py:127-156`` adds every posting); here the first occurrence keeps
+    its place and its weight becomes the fp32 sum of all occurrences, left to right in
+    row order.  Rows without repeats are returned as they are."""
+    indptr = np.asarray(indptr, dtype=np.int64)
+    indices = np.asarray(indices, dtype=np.int32)
+    data = np.asarray(data, dtype=np.float32)
+    n = len(indptr) - 1
+    if n <= 0 or len(indices) == 0:
+        return indptr, indices, data
+    rows = np.repeat(np.arange(n, dtype=np.int64), np.diff(indptr))
+    lo = min(0, int(indices.min()))
+    span = int(indices.max()) + 1 - lo
+    sk = np.sort(rows * span + (indices.astype(np.int64) - lo))
+    dup_rows = np.unique(sk[1:][sk[1:] == sk[:-1]] // span)
+    if len(dup_rows) == 0:
+        return indptr, indices, data
+    keep = np.ones(len(indices), dtype=bool)
+    out_data = data.copy()
+    for r in dup_rows:
+        e0, e1 = int(indptr[r]), int(indptr[r + 1])
+        first = {}
+        for e in range(e0, e1):
+            t = int(indices[e])
+            if t in first:
+                f = first[t]
+                out_data[f] = np.float32(out_data[f] + data[e])
+                keep[e] = False
+            else:
+                first[t] = e
+    new_nnz = np.bincount(rows[keep], minlength=n)
+    new_ip = np.zeros(n + 1, dtype=np.int64)
+    np.cumsum(new_nnz, out=new_ip[1:])
+    return new_ip, indices[keep], out_data[keep]
+
+
 def build_index(indptr: np.ndarray, indices: np.ndarray, data: np.ndarray, V: int) -> Index:
     """The same layout as build_index_reference via the C stable counting sort."""
     L = lib()
@@ -337,7 +376,7 @@ def score_full(index: Index, qi: np.ndarray, qs: np.ndarray, weights=None,
     return out
 
 
-def score_dense_f64(indptr, indices, data, V: int, qi, qs) -> np.ndarray:
+def score_dense_f64(indptr, indices, data, V: int, qi, qs, nthreads: int | None = None) -> np.ndarray:
     L = lib()
     indptr = np.ascontiguousarray(indptr, dtype=np.int64)
     indices = np.ascontiguousarray(indices, dtype=np.int32)
@@ -348,7 +387,7 @@ def score_dense_f64(indptr, indices, data, V: int, qi, qs) -> np.ndarray:
     N = len(indptr) - 1
     out = np.zeros((B, N), dtype=np.float64)
     assert L.orc_score_dense_f64(N, V, _p(indptr), _p(indices), _p(data), B, W, _p(qi), _p(qs),
-                                 _p(out)) == 0
+                                 _p(out), nthreads or nthreads_default()) == 0
     return out
 
 

@@ -10,7 +10,7 @@ import pytest
 import torch
 
 from oracle import oracle as O
-from parity import assert_bit_exact
+from parity import assert_bit_exact, check_topk
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -86,10 +86,9 @@ def test_errors_are_loud():
         gpusparse.triton_fused_score(g, t(qi), t(qs[:, :3]))
     with pytest.raises(ValueError):
         gpusparse.triton_fused_score(g, t(qi), t(qs), top_k=0)
-    big = O.synth_csr(20000, 30522, seed=18)
-    gb = gpusparse.build_from_csr_tensors(t(big[0]), t(big[1]), t(big[2]), 30522, DEV)
-    with pytest.raises(RuntimeError):                        # beyond the supported top-k
-        gpusparse.triton_fused_score(gb, t(qi), t(qs), top_k=9000)
+    with pytest.raises(RuntimeError):                        # more scored terms than a plan holds
+        gpusparse.triton_fused_score(g, t(np.zeros((1, 16385), np.int32)),
+                                     t(np.ones((1, 16385), np.float32)), top_k=5)
 
 
 def _stub_harness():
@@ -139,15 +138,80 @@ def test_plugin_retrieve_chunked_path_and_run_file(tmp_path):
     assert len(lines) == sum(len(r) for r in mono)
 
 
-def test_duplicate_doc_term_entries_are_refused():
-    """A term listed twice in one CSR row would repeat a doc id inside its posting list;
-    the scorer updates a list's documents in parallel, so the build refuses it."""
+def _with_duplicates(ip, ix, dt, seed):
+    """A copy of a CSR in which some rows list a term two or three times (adjacent and
+    apart), with weights that do not sum exactly in fp32."""
+    rng = np.random.default_rng(seed)
+    ix, dt = ix.copy(), dt.copy()
+    n = len(ip) - 1
+    for r in rng.choice(n, size=max(1, n // 20), replace=False):
+        e0, e1 = int(ip[r]), int(ip[r + 1])
+        if e1 - e0 < 4:
+            continue
+        j = rng.integers(e0 + 1, e1)
+        ix[j] = ix[e0]                          # a repeat of the row's first term
+        dt[j] = np.float32(rng.random() * 3.0)
+        if e1 - e0 > 40 and r % 2:
+            ix[e1 - 1] = ix[e0]                 # and a third occurrence at the row's end
+            dt[e1 - 1] = np.float32(0.1)
+    return ix, dt
+
+
+def test_duplicate_doc_term_entries_are_merged():
+    """A term listed more than once in one CSR row: the reference keeps every entry as a
+    posting and its scatter-add sums them.  The build merges them (first position, fp32 sum
+    of the weights in row order); the index equals the oracle's build of the merged CSR,
+    scores are bit-exact against the oracle and within tolerance of the fp64 scores of the
+    original CSR, through the tensor builder, the streamed builder (chunk indptr not
+    starting at 0) and the plug-in's scipy path."""
+    import scipy.sparse as sp
     import gpusparse
-    ip, ix, dt = O.synth_csr(50, 30522, seed=21)
-    ix = ix.copy()
-    ix[ip[3] + 1] = ix[ip[3]]                                 # doc 3 lists one term twice
-    with pytest.raises(ValueError, match="twice"):
-        gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), 30522, DEV)
+    from run_correctness_verification import build_gpu_index_from_csr
+    V = 30522
+    ip, ix0, dt0 = O.synth_csr(3000, V, seed=21)
+    ix, dt = _with_duplicates(ip, ix0, dt0, 5)
+    mip, mix, mdt = O.merge_duplicates(ip, ix, dt)
+    assert len(mix) < len(ix)
+    oidx = O.build_index(mip, mix, mdt, V)
+    qi, qs = O.synth_queries(40, V, seed=22)
+    S = O.score_dense_f64(ip, ix, dt, V, qi, qs)
+    ipd, ixd, dtd = t(ip), t(ix), t(dt)
+    builds = {
+        "tensors": gpusparse.build_from_csr_tensors(ipd, ixd, dtd, V, DEV),
+        "streamed": gpusparse.build_streamed(
+            3000, V, lambda lo, hi, wd: (ipd[lo:hi + 1], ixd, dtd if wd else None), DEV,
+            chunk_docs=1024),
+        "scipy": build_gpu_index_from_csr(sp.csr_matrix((dt, ix, ip), shape=(3000, V)), DEV),
+    }
+    for name, g in builds.items():
+        assert np.array_equal(g.doc_ids.cpu().numpy(), oidx.doc_ids), name
+        assert np.array_equal(g.scores.cpu().numpy().view(np.uint32), oidx.scores.view(np.uint32)), name
+        s, i = gpusparse.triton_fused_score(g, t(qi), t(qs), top_k=500)
+        rs, ri = O.score_topk(oidx, qi, qs, 500, head=g.head_ids.cpu().numpy())
+        assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
+        check_topk(s.cpu().numpy(), i.cpu().numpy(), S, 500)
+
+
+def test_merge_duplicates_kernel_matches_oracle():
+    """gsp_csr_dedup_* against the oracle's merge on rows of many lengths (up to 700
+    entries, terms repeated up to 40 times) and a chunk whose indptr starts above 0."""
+    from gpusparse.index import merge_duplicates
+    rng = np.random.default_rng(7)
+    lens = rng.integers(0, 700, size=400)
+    lens[:5] = [0, 1, 33, 64, 65]
+    ip = np.zeros(len(lens) + 1, dtype=np.int64)
+    np.cumsum(lens, out=ip[1:])
+    ix = rng.integers(0, 60, size=int(ip[-1])).astype(np.int32)     # many repeats per row
+    dt = rng.random(int(ip[-1])).astype(np.float32)
+    for lo, hi in [(0, 400), (37, 211)]:
+        sub_ip = ip[lo:hi + 1]
+        got = merge_duplicates(t(sub_ip), t(ix), t(dt))
+        exp = O.merge_duplicates(sub_ip - sub_ip[0], ix[sub_ip[0]:sub_ip[-1]], dt[sub_ip[0]:sub_ip[-1]])
+        assert np.array_equal(got[0].cpu().numpy(), exp[0])
+        assert np.array_equal(got[1].cpu().numpy(), exp[1])
+        assert np.array_equal(got[2].cpu().numpy().view(np.uint32), exp[2].view(np.uint32))
+        only_ix = merge_duplicates(t(sub_ip), t(ix), None)
+        assert np.array_equal(only_ix[1].cpu().numpy(), exp[1]) and only_ix[2] is None
 
 
 def test_reference_style_index_with_repeated_doc_is_refused():

@@ -93,24 +93,22 @@ def _drop_zeros(ip, ix, dt):
     return nip, ix[keep][order], dt[keep][order]
 
 
-def test_duplicate_terms_in_a_document_are_refused():
-    """The reference's builder would keep both postings (a list that repeats doc 0); the
-    scorer updates a list's documents in parallel, so this build refuses such a CSR with
-    ValueError instead of scoring it wrongly.  Merged duplicates build normally."""
+def test_duplicate_terms_in_a_document_are_merged():
+    """The reference's builder keeps both postings of a term a row lists twice (a list that
+    repeats doc 0) and its scatter-add sums them; this build merges them first (weights
+    summed in row order), which gives the index of the scipy-summed CSR."""
     import gpusparse
     ip = np.array([0, 3, 5], dtype=np.int64)
     ix = np.array([4, 4, 1, 4, 2], dtype=np.int32)
     dt = np.array([0.5, 0.25, 1.0, 2.0, 3.0], dtype=np.float32)
     t = lambda a: torch.from_numpy(a).to(DEV)  # noqa: E731
-    with pytest.raises(ValueError, match="twice"):
-        gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), 8, DEV)
+    idx = gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), 8, DEV)
     m = sp.csr_matrix((dt, ix, ip), shape=(2, 8))
     m.sum_duplicates()
-    idx = gpusparse.build_from_csr_tensors(t(m.indptr.astype(np.int64)), t(m.indices.astype(np.int32)),
-                                           t(m.data.astype(np.float32)), 8, DEV)
     ref = O.build_index_reference(m, 8)
     assert np.array_equal(idx.doc_ids.cpu().numpy(), ref.doc_ids)
     assert np.array_equal(idx.scores.cpu().numpy(), ref.scores)
+    assert float(idx.scores.cpu().numpy()[0]) == 0.75         # doc 0, term 4: 0.5 + 0.25
 
 
 def test_bad_column_id_raises():

@@ -46,8 +46,10 @@ def test_layout_invariant_at_scale(big):
     import gpusparse._lib as L
     index, _ = big
     bad, dup = ctypes.c_int64(-1), ctypes.c_int64(-1)
+    ws = L.workspace(L.CHECK_WS_BYTES, DEV)
     L.check(L.lib().gsp_check_sorted(V, L.ptr(index.doc_ids), L.ptr(index.offsets), L.ptr(index.lengths),
-                                     ctypes.byref(bad), ctypes.byref(dup), L.stream_of(DEV)), "check")
+                                     ctypes.byref(bad), ctypes.byref(dup), L.ptr(ws), ws.numel(),
+                                     L.stream_of(DEV)), "check")
     assert bad.value == 0 and dup.value == 0
 
 

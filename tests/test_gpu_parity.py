@@ -202,23 +202,71 @@ def test_shards_merge_equals_unsharded(corpus):
         assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
 
 
-def test_supported_limits_max_k_and_max_width(corpus, gindex):
-    """top_k = 8192 and W = 4096 (the supported maxima) stay exact; W = 4097 is refused."""
+@pytest.mark.parametrize("k", [8192, 8193, 12000, 20000])
+def test_large_k_is_exact(corpus, gindex, k):
+    """top_k at and above the 8192 keys one CTA sorts in shared memory (the reference's
+    torch.topk takes any k): above it every key is written out and each query's top-k is
+    radix-selected and merge-sorted in global memory; k = 20000 is the whole corpus."""
     import gpusparse
     _, _, _, oidx = corpus
-    qi, qs = O.synth_queries(8, V, seed=50)
-    s, i = gpusparse.triton_fused_score(gindex, t(qi), t(qs), top_k=8192)
-    rs, ri = O.score_topk(oidx, qi, qs, 8192, head=hd(gindex))
+    qi, qs = O.synth_queries(12, V, seed=50)
+    s, i = gpusparse.triton_fused_score(gindex, t(qi), t(qs), top_k=k)
+    rs, ri = O.score_topk(oidx, qi, qs, k, head=hd(gindex))
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
+
+
+def test_large_k_through_the_shard_merge_and_compacted_topk(corpus):
+    """k above 8192 in the other two selections: merging doc-range shards' keys
+    (gsp_merge_topk) and compacted_topk over a dense score matrix."""
+    import gpusparse
+    from gpusparse.distributed import ShardLayout
+    ip, ix, dt, oidx = corpus
+    N, k = 20000, 9000
+    qi, qs = O.synth_queries(6, V, seed=52)
+    g0 = gpusparse.build_from_csr_tensors(t(ip), t(ix), t(dt), V, DEV)
+    head = g0.head_ids.cpu().numpy()
+    keys = []
+    for r in range(2):
+        lay = ShardLayout(N, 2, r)
+        g = gpusparse.build_from_csr_tensors(t(ip[lay.lo:lay.hi + 1] - ip[lay.lo]),
+                                             t(ix[ip[lay.lo]:ip[lay.hi]]), t(dt[ip[lay.lo]:ip[lay.hi]]),
+                                             V, DEV, doc_base=lay.lo, head_ids=head)
+        keys.append(gpusparse.score_topk(g, t(qi), t(qs), k, with_keys=True)[2])
+    s, i = gpusparse.merge_topk(torch.stack(keys), ShardLayout(N, 2, 0).list_counts(k), k)
+    rs, ri = O.score_topk(oidx, qi, qs, k, head=head)
+    assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
+    S = O.score_full(oidx, qi, qs, head=head)
+    tau = np.full(6, -np.inf, dtype=np.float32)
+    tau[1] = np.float32(np.sort(S[1])[-8500])   # fewer than k survive: padded with (-inf, 0)
+    v, c = gpusparse.compacted_topk(t(S), t(tau), k)
+    ov, oc = O.compacted_topk(S, tau, k)
+    assert np.array_equal(v.cpu().numpy(), ov) and np.array_equal(c.cpu().numpy(), oc)
+
+
+def test_wide_queries(corpus, gindex):
+    """W = 16384 scored slots (the most one query plan sorts) stays exact; a batch padded
+    wider than that is compacted to its longest query first (same result); a query with
+    more than 16384 scored terms is refused."""
+    import gpusparse
+    _, _, _, oidx = corpus
     rng = np.random.default_rng(51)
-    wi = rng.integers(0, V, size=(4, 4096)).astype(np.int32)
-    ws = rng.random((4, 4096)).astype(np.float32)
+    wi = rng.integers(0, V, size=(3, 16384)).astype(np.int32)
+    ws = rng.random((3, 16384)).astype(np.float32)
     s, i = gpusparse.triton_fused_score(gindex, t(wi), t(ws), top_k=100)
     rs, ri = O.score_topk(oidx, wi, ws, 100, head=hd(gindex))
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
+    qi, qs = O.synth_queries(5, V, seed=53)
+    pi = np.full((5, 20000), -1, dtype=np.int32)
+    ps = np.zeros((5, 20000), dtype=np.float32)
+    for b in range(5):   # the query's slots spread over the wide row, padding between them
+        cols = np.sort(rng.choice(20000, size=qi.shape[1], replace=False))
+        pi[b, cols], ps[b, cols] = qi[b], qs[b]
+    s, i = gpusparse.triton_fused_score(gindex, t(pi), t(ps), top_k=1000)
+    rs, ri = O.score_topk(oidx, qi, qs, 1000, head=hd(gindex))
+    assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
     with pytest.raises(RuntimeError):
-        gpusparse.triton_fused_score(gindex, t(np.zeros((2, 4097), np.int32)),
-                                     t(np.zeros((2, 4097), np.float32)), top_k=10)
+        gpusparse.triton_fused_score(gindex, t(np.zeros((2, 16385), np.int32)),
+                                     t(np.ones((2, 16385), np.float32)), top_k=10)
 
 
 @pytest.mark.parametrize("N", [1, 4097, 20000])

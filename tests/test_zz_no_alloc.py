@@ -68,10 +68,10 @@ def test_noalloc_refuses_batches_beyond_its_scratch():
 
 
 def test_noalloc_minimum_capacity_stresses_the_candidate_protocol():
-    """A large batch (300 queries, k = 1000) makes the fixed scratch shrink every query's
-    candidate buffers to their minimum, so a buffer fills after about one tile of
-    candidates: many compactions, generations and retries against raised thresholds.
-    The result must still equal the workspace entry point (larger buffers) bit for bit."""
+    """A large batch (300 queries, k = 1000) at the minimum candidate capacity (k + 1024
+    keys, which at k = 1000 is also the default), so a buffer fills after about one tile
+    of candidates: many compactions, generations and retries against raised thresholds.
+    The result must still equal the workspace entry point bit for bit."""
     import gpusparse
     import gpusparse._lib as L
     from gpusparse import synth
@@ -80,6 +80,26 @@ def test_noalloc_minimum_capacity_stresses_the_candidate_protocol():
     qi, qs = synth.synth_queries(300, V, seed=27, device=DEV)
     ref_s, ref_i = gpusparse.score_topk(index, qi, qs, 1000)
     rc, s, i = noalloc(index, qi, qs, 1000)
+    L.check(rc, "gsp_score_topk_noalloc")
+    torch.cuda.synchronize()
+    assert not torch.isnan(s).any()
+    assert torch.equal(i, ref_i)
+    assert torch.equal(s.view(torch.int32), ref_s.view(torch.int32))
+
+
+def test_noalloc_shrinks_candidate_buffers_above_k_2048():
+    """k = 4096: the default candidate capacity (k + k/2) is above the minimum (k + 1024),
+    and 130 queries fit the fixed scratch only once the buffers shrink to that minimum; the
+    shrunken buffers compact more often and must still give the workspace result bit for
+    bit."""
+    import gpusparse
+    import gpusparse._lib as L
+    from gpusparse import synth
+    ip, ix, dt = synth.synth_csr(60_000, V, seed=28, device=DEV)
+    index = gpusparse.build_from_csr_tensors(ip, ix, dt, V, DEV)
+    qi, qs = synth.synth_queries(130, V, seed=29, device=DEV)
+    ref_s, ref_i = gpusparse.score_topk(index, qi, qs, 4096)
+    rc, s, i = noalloc(index, qi, qs, 4096)
     L.check(rc, "gsp_score_topk_noalloc")
     torch.cuda.synchronize()
     assert not torch.isnan(s).any()
