@@ -75,6 +75,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--k", type=int, default=1000)
     ap.add_argument("--wdtype", choices=["fp32", "bf16", "u8"], default=None)
+    ap.add_argument("--head-mode", choices=["auto", "cuda", "tc"], default="auto",
+                    help="head terms: the library's choice, the CUDA cores (canonical order) or "
+                         "the tensor cores (tcgen05, 3xTF32)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="target CPU work of the bounded CPU-baseline sample")
@@ -239,6 +242,8 @@ def run_ours(args):
     wl = workload(args)
     N, B, k, wd = wl["num_docs"], wl["batch"], wl["k"], wl["wdtype"]
     lay = ShardLayout(N, world, rank)
+    head_code = {"auto": L.HEAD_AUTO, "cuda": L.HEAD_CUDA_CORES, "tc": L.HEAD_TENSOR_CORES}[args.head_mode]
+    L.check(L.lib().gsp_set_head_mode(head_code), "head mode")
     dlaw = synth.Law(zipf_s=wl["zipf_s"])
     qlaw = synth.Law(zipf_s=wl["zipf_s"], nnz_mean=30.0, nnz_sd=15.0, nnz_lo=5, nnz_hi=128,
                      min_nnz_item0=107)
@@ -402,6 +407,8 @@ def run_ours(args):
                    (" + NCCL all-to-all of query blocks, merge, all-gather" if world > 1 else ""),
                    "l2": "inputs larger than L2 (index >> 126 MB); no flush",
                    "index_build_s": round(build_s, 2),
+                   "head_terms": {"auto": "library choice (CUDA cores)", "cuda": "CUDA cores",
+                                  "tc": "tensor cores (tcgen05, 3xTF32)"}[args.head_mode],
                    **({"threshold_sharing": sharing} if sharing else {})},
         "gpu_launches": launches_per_step * K,
         **({"single_query_latency": {"batch": 1, "k": k, "p50_ms": lat1,

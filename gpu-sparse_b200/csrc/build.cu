@@ -371,6 +371,19 @@ __global__ void dedup_fill_kernel(int64_t n_rows, const int64_t* __restrict__ in
   }
 }
 
+// lo = x - (x with its low 13 mantissa bits cleared): exact in fp32
+__global__ void head_lo_kernel(int64_t n, const float4* __restrict__ rows, float4* __restrict__ lo) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const float4 v = rows[i];
+    float4 r;
+    r.x = __fsub_rn(v.x, __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u));
+    r.y = __fsub_rn(v.y, __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u));
+    r.z = __fsub_rn(v.z, __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u));
+    r.w = __fsub_rn(v.w, __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u));
+    lo[i] = r;
+  }
+}
+
 int64_t n_blocks_of(int64_t n_docs, int32_t block_docs) {
   return (n_docs + block_docs - 1) / block_docs;
 }
@@ -599,6 +612,19 @@ extern "C" int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t
               GSP_ERR_ARG, "gsp_index_quantize: bad arguments");
   quant_kernel<<<unsigned((int64_t(V) * 32 + 255) / 256), 256, 0, as_stream(stream)>>>(
       V, offsets, padded, max_scores, weights, wdtype, out_weights, term_scale);
+  GSP_CHECK_LAUNCH();
+  return GSP_OK;
+}
+
+extern "C" int gsp_index_head_lo(int64_t n, const float* rows, float* lo, void* stream) {
+  GSP_REQUIRE(n >= 0 && n % 4 == 0 && (n == 0 || (rows && lo)) && (reinterpret_cast<uintptr_t>(rows) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(lo) & 15) == 0,
+              GSP_ERR_ARG, "gsp_index_head_lo: bad arguments (n a multiple of 4, 16-byte aligned arrays)");
+  if (n == 0) return GSP_OK;
+  const int64_t n4 = n / 4;
+  const int64_t blocks = std::min<int64_t>((n4 + 255) / 256, int64_t(num_sms()) * 16);
+  head_lo_kernel<<<unsigned(blocks), 256, 0, as_stream(stream)>>>(n4, reinterpret_cast<const float4*>(rows),
+                                                                 reinterpret_cast<float4*>(lo));
   GSP_CHECK_LAUNCH();
   return GSP_OK;
 }

@@ -58,6 +58,9 @@
 // oracle's canonical order.
 #include "common.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <atomic>
 #include <mutex>
@@ -801,6 +804,198 @@ __global__ void final_counts_kernel(int32_t B, int32_t k, const unsigned long lo
   counts[3 * q + 2] = b == 1 ? done[2 * q + 1] : 0;
 }
 
+// Steps 2 and 3 of one work item (query q, tile b), after the head terms are in acc: the
+// tail runs scattered into the shared-memory accumulators in ascending term id, then the
+// selection of the launch's mode.  Shared by the CUDA-core scorer and the tensor-core one.
+template <typename WT, int kMode>
+__device__ __forceinline__ void item_tail_select(const ScoreParams& p, const int32_t q, const int32_t b,
+                                                 float* __restrict__ acc, uint32_t* __restrict__ hist) {
+  const int lane = lane_id();
+  const WT* __restrict__ wts = static_cast<const WT*>(p.weights);
+  const int32_t* __restrict__ doc_ids = p.doc_ids;
+  const int64_t pbase = int64_t(q) * p.ecap;
+  const int32_t nr = p.n_runs[q];
+  const int32_t* __restrict__ run_term = p.run_term + pbase;
+  const uint32_t* __restrict__ run_b32 = p.run_base32 + pbase;
+  const uint16_t* __restrict__ run_end = p.run_end + pbase;
+  const float* __restrict__ run_w0 = p.run_w0 + pbase;
+  const float* __restrict__ ent_w = p.ent_w + pbase;
+  const int32_t d0i = b * kTile;
+  const int32_t d1 = int32_t(min64(int64_t(b + 1) * kTile, p.n_docs));
+  const uint32_t span = uint32_t(d1 - d0i);
+  const unsigned long long g_pub = __ldcg(p.gthr + q);   // consumed by the selection
+  unsigned long long bnd = ~0ull;                        // lane s: shard s's row
+  if (p.n_shards > 1 && lane < p.n_shards) bnd = __ldcg(p.board + int64_t(lane) * p.B + q);
+
+  // 2. tail runs in ascending term id
+  const uint32_t* __restrict__ brow = p.block_starts + int64_t(b) * kTileBlocksI * p.V;
+  const uint32_t* __restrict__ brow_end =
+      p.block_starts + int64_t(min((b + 1) * kTileBlocksI, p.n_iblocks)) * p.V;
+  for (int32_t rb = 0; rb < nr; rb += 32) {
+    const int32_t ri = rb + lane;
+    uint32_t lo = 0, hi = 0, b32 = 0;
+    int32_t e0 = 0, ne = 0;
+    float w0 = 0.f, scale = 1.0f;
+    if (ri < nr) {
+      const int32_t t = run_term[ri];
+      lo = __ldg(brow + t);
+      hi = __ldg(brow_end + t);
+      e0 = ri ? int32_t(run_end[ri - 1]) : 0;
+      ne = int32_t(run_end[ri]) - e0;
+      b32 = run_b32[ri];
+      w0 = run_w0[ri];
+      if constexpr (std::is_same<WT, uint8_t>::value) scale = __ldg(p.term_scale + t);
+    }
+    const int32_t n = int32_t(hi - lo);
+    const uint32_t act = __ballot_sync(FULL, n > 0);
+    const uint32_t lng = __ballot_sync(FULL, n > 0 && (n >= kLongRun || ne > 1));
+    int c = 0;  // next run (lane) to process
+    while (c < 32) {
+      const uint32_t from = c ? ~((1u << c) - 1u) : FULL;
+      if (!(act & from)) break;
+      const uint32_t nl = lng & from;
+      const int next_long = nl ? __ffs(nl) - 1 : 32;
+      const uint32_t upto = next_long < 32 ? ((1u << next_long) - 1u) : FULL;
+      const uint32_t seg = act & ~lng & from & upto;
+      if (seg) {
+        // consecutive short runs flattened into full 32-lane chunks
+        const int m = __popc(seg);
+        const int src = lane < m ? int(__fns(seg, 0, lane + 1)) : 0;
+        const int32_t n_c = __shfl_sync(FULL, n, src);
+        const uint32_t lo_c = __shfl_sync(FULL, lo, src), b32_c = __shfl_sync(FULL, b32, src);
+        const float w_c = __shfl_sync(FULL, w0, src), s_c = __shfl_sync(FULL, scale, src);
+        const int32_t sz = lane < m ? n_c : 0;
+        int32_t incl = sz;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int32_t y = __shfl_up_sync(FULL, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const int32_t P = incl - sz;
+        const int32_t total = __shfl_sync(FULL, incl, 31);
+        for (int32_t F = 0; F < total; F += 32) {
+          const int32_t f = F + lane;
+          const bool valid = f < total;
+          const uint32_t bit = (lane < m && P >= F && P < F + 32) ? (1u << (P - F)) : 0u;
+          const uint32_t S = __reduce_or_sync(FULL, bit);
+          const int jF = __popc(__ballot_sync(FULL, lane < m && P <= F)) - 1;
+          int j = jF + __popc(S & (lanemask_lt() | (1u << lane)) & ~1u);
+          j = valid ? j : 0;
+          const int32_t Pj = __shfl_sync(FULL, P, j);
+          const uint32_t loj = __shfl_sync(FULL, lo_c, j), bj = __shfl_sync(FULL, b32_c, j);
+          const float wj = __shfl_sync(FULL, w_c, j), sj = __shfl_sync(FULL, s_c, j);
+          int32_t col = -1;
+          float wv = 0.f;
+          if (valid) {
+            const int64_t pos = (int64_t(bj) << 5) + loj + (f - Pj);
+            col = __ldg(doc_ids + pos) - d0i;
+            wv = WDecode<WT>::get(wts, pos, sj);
+          }
+          // lanes on the same document (different terms) apply in term (= lane) order
+          const int32_t dkey = (valid && uint32_t(col) < span) ? col : -1 - lane;
+          const uint32_t peers = __match_any_sync(FULL, dkey);
+          const int rank = __popc(peers & lanemask_lt());
+          const int top = int(__reduce_max_sync(FULL, uint32_t(rank)));
+          for (int rr = 0; rr <= top; ++rr) {
+            if (rank == rr) acc_add(acc, col, span, wj, wv);
+            __syncwarp();
+          }
+        }
+      }
+      if (next_long >= 32) break;
+      // one long (or multi-entry) run
+      const int jl = next_long;
+      const int32_t nl_n = __shfl_sync(FULL, n, jl);
+      const uint32_t lo_l = __shfl_sync(FULL, lo, jl), b32_l = __shfl_sync(FULL, b32, jl);
+      const int32_t e0_l = __shfl_sync(FULL, e0, jl), ne_l = __shfl_sync(FULL, ne, jl);
+      const float w0_l = __shfl_sync(FULL, w0, jl), sc_l = __shfl_sync(FULL, scale, jl);
+      const int64_t base = (int64_t(b32_l) << 5) + lo_l;
+      if (ne_l == 1 && nl_n <= 64) {
+        // the next run, if it is long with one entry and nothing lies between: as a pair
+        const uint32_t after = act & ~((2u << jl) - 1u);
+        const int j2 = after ? __ffs(after) - 1 : 32;
+        if (j2 < 32 && ((lng >> j2) & 1u)) {
+          const int32_t n2 = __shfl_sync(FULL, n, j2), ne2 = __shfl_sync(FULL, ne, j2);
+          const uint32_t lo2 = __shfl_sync(FULL, lo, j2), b322 = __shfl_sync(FULL, b32, j2);
+          const float w02 = __shfl_sync(FULL, w0, j2), sc2 = __shfl_sync(FULL, scale, j2);
+          if (ne2 == 1 && n2 <= 64) {
+            const int64_t base2 = (int64_t(b322) << 5) + lo2;
+            run_pair<WT>(doc_ids + base, wts + base, sc_l, nl_n, w0_l, doc_ids + base2, wts + base2, sc2, n2,
+                         w02, d0i, span, acc);
+            c = j2 + 1;
+            continue;
+          }
+        }
+      }
+      if (ne_l == 1) {
+        run_window<WT, 1>(doc_ids + base, wts + base, sc_l, nl_n, d0i, span, acc, w0_l, 0.f, nullptr, 0);
+      } else if (ne_l == 2) {
+        run_window<WT, 2>(doc_ids + base, wts + base, sc_l, nl_n, d0i, span, acc, w0_l, ent_w[e0_l + 1],
+                          nullptr, 0);
+      } else {
+        run_window<WT, 0>(doc_ids + base, wts + base, sc_l, nl_n, d0i, span, acc, 0.f, 0.f, ent_w + e0_l,
+                          ne_l);
+      }
+      c = jl + 1;
+    }
+  }
+  __syncwarp();
+
+  // 3. fused selection: the documents whose score reaches the query's threshold go to
+  // its candidate buffer (a superset of the keys >= threshold is harmless: only the k
+  // largest survive the compactions and the merge)
+  uint64_t thr = uint64_t(g_pub);
+  if (p.n_shards > 1) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) bnd = min(bnd, __shfl_xor_sync(FULL, bnd, o));
+    thr = max(thr, uint64_t(bnd));
+  }
+  if constexpr (kMode == kModeTree) {
+    // small-batch mode (one selection pass per tile): the tile's own exact top-k
+    tile_topk(acc, span, uint32_t(p.doc_base + d0i), min(p.tile_k, int32_t(span)), p.tile_k, hist,
+              p.tile_out + (int64_t(q) * p.n_blocks + b) * p.tile_k);
+  } else if constexpr (kMode == kModeDense) {
+    // every document's key (lane writes columns 128 i + 4 lane .. + 3, two 16-byte stores)
+    uint64_t* __restrict__ row = p.dense + int64_t(q - p.q_lo) * p.dense_ld + d0i;
+    const uint32_t dbase = uint32_t(p.doc_base + d0i);
+#pragma unroll
+    for (int i = 0; i < kTile / 128; ++i) {
+      const uint32_t c = uint32_t(128 * i + 4 * lane);
+      const float4 v = *reinterpret_cast<const float4*>(acc + c);
+      ulonglong2 k0, k1;
+      k0.x = c + 0 < span ? pack_key(v.x, dbase + c + 0) : 0ull;
+      k0.y = c + 1 < span ? pack_key(v.y, dbase + c + 1) : 0ull;
+      k1.x = c + 2 < span ? pack_key(v.z, dbase + c + 2) : 0ull;
+      k1.y = c + 3 < span ? pack_key(v.w, dbase + c + 3) : 0ull;
+      *reinterpret_cast<ulonglong2*>(row + c) = k0;
+      *reinterpret_cast<ulonglong2*>(row + c + 2) = k1;
+    }
+  } else {
+#pragma unroll
+  for (int h = 0; h < kTile / kSel; ++h) {
+    if (uint32_t(h * kSel) >= span) break;
+    const uint32_t sp = min(span - uint32_t(h * kSel), uint32_t(kSel));
+    const uint32_t m = mark_tile(acc + h * kSel, lane, sp, thr);
+    if (__any_sync(FULL, m != 0u)) {
+      QueryBuf qb{p.cand + int64_t(q) * 3 * p.cand_stride, p.cand_stride, p.gthr + q, p.rg + q,
+                  p.done + 2 * q, p.cdone + q, p.fault, p.cap, p.k, p.wait_limit, p.kg};
+      const uint64_t pub =
+          append_candidates(qb, acc + h * kSel, sp, uint32_t(p.doc_base + d0i + h * kSel), hist, thr, m);
+      // this shard's row of every board: local, then the peers' (remote reductions over
+      // NVLink; nothing waits on them)
+      if (pub != 0ull) {
+        const int64_t slot = int64_t(p.shard) * p.B + q;
+        if (lane == 0) atomicMax(p.board + slot, (unsigned long long)pub);
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) {
+          if (r < p.n_peers && lane == r + 1) atomicMax(p.peer_thr[r] + slot, (unsigned long long)pub);
+        }
+      }
+    }
+  }
+  }
+}
+
 // WT: posting weight type; HT: head row type (WT, or float rows for uint8 postings);
 // kMode: kModeBuffers, kModeTree (per-tile top-k lists instead of the shared candidate
 // buffers) or kModeDense (every key written out).
@@ -812,9 +1007,7 @@ score_kernel(const ScoreParams p) {
   unsigned char* wsm = smem + size_t(wid) * WarpLayout::total;
   float* acc = reinterpret_cast<float*>(wsm + WarpLayout::acc);
   uint32_t* hist = reinterpret_cast<uint32_t*>(wsm + WarpLayout::hist);
-  const WT* __restrict__ wts = static_cast<const WT*>(p.weights);
   const HT* __restrict__ hrows = static_cast<const HT*>(p.head_rows);
-  const int32_t* __restrict__ doc_ids = p.doc_ids;
   const unsigned long long n_items = (unsigned long long)p.q_n * unsigned(p.n_blocks);
   unsigned long long nit = 0;   // the claimed item (lane 0)
   if (lane == 0) nit = atomicAdd(p.item_next, 1ull);
@@ -829,19 +1022,11 @@ score_kernel(const ScoreParams p) {
     const int32_t q = p.q_lo + int32_t(it32 - uint32_t(b) * uint32_t(p.q_n));
     const int64_t pbase = int64_t(q) * p.ecap;
     const int32_t nhe = p.n_head_e[q];
-    const int32_t nr = p.n_runs[q];
     const uint16_t* __restrict__ head_h = p.head_h + pbase;
     const float* __restrict__ head_w = p.head_w + pbase;
     const float* __restrict__ head_sc = p.head_scale + pbase;
-    const int32_t* __restrict__ run_term = p.run_term + pbase;
-    const uint32_t* __restrict__ run_b32 = p.run_base32 + pbase;
-    const uint16_t* __restrict__ run_end = p.run_end + pbase;
-    const float* __restrict__ run_w0 = p.run_w0 + pbase;
-    const float* __restrict__ ent_w = p.ent_w + pbase;
     {
       const int32_t d0i = b * kTile;
-      const int32_t d1 = int32_t(min64(int64_t(b + 1) * kTile, p.n_docs));
-      const uint32_t span = uint32_t(d1 - d0i);
 
       // 1. head rows, accumulators in registers: in each of the kHeadParts parts of the
       // tile, lane owns documents part * kTile / kHeadParts + 128 * i + 4 * lane + j
@@ -867,186 +1052,18 @@ score_kernel(const ScoreParams p) {
         for (int i = 0; i < kHeadVec; ++i) *reinterpret_cast<float4*>(acc + pofs + 128 * i + 4 * lane) = a[i];
       }
       __syncwarp();
-      const unsigned long long g_pub = __ldcg(p.gthr + q);   // consumed by the selection
-      unsigned long long bnd = ~0ull;                        // lane s: shard s's row
-      if (p.n_shards > 1 && lane < p.n_shards) bnd = __ldcg(p.board + int64_t(lane) * p.B + q);
-
-      // 2. tail runs in ascending term id
-      const uint32_t* __restrict__ brow = p.block_starts + int64_t(b) * kTileBlocksI * p.V;
-      const uint32_t* __restrict__ brow_end =
-          p.block_starts + int64_t(min((b + 1) * kTileBlocksI, p.n_iblocks)) * p.V;
-      for (int32_t rb = 0; rb < nr; rb += 32) {
-        const int32_t ri = rb + lane;
-        uint32_t lo = 0, hi = 0, b32 = 0;
-        int32_t e0 = 0, ne = 0;
-        float w0 = 0.f, scale = 1.0f;
-        if (ri < nr) {
-          const int32_t t = run_term[ri];
-          lo = __ldg(brow + t);
-          hi = __ldg(brow_end + t);
-          e0 = ri ? int32_t(run_end[ri - 1]) : 0;
-          ne = int32_t(run_end[ri]) - e0;
-          b32 = run_b32[ri];
-          w0 = run_w0[ri];
-          if constexpr (std::is_same<WT, uint8_t>::value) scale = __ldg(p.term_scale + t);
-        }
-        const int32_t n = int32_t(hi - lo);
-        const uint32_t act = __ballot_sync(FULL, n > 0);
-        const uint32_t lng = __ballot_sync(FULL, n > 0 && (n >= kLongRun || ne > 1));
-        int c = 0;  // next run (lane) to process
-        while (c < 32) {
-          const uint32_t from = c ? ~((1u << c) - 1u) : FULL;
-          if (!(act & from)) break;
-          const uint32_t nl = lng & from;
-          const int next_long = nl ? __ffs(nl) - 1 : 32;
-          const uint32_t upto = next_long < 32 ? ((1u << next_long) - 1u) : FULL;
-          const uint32_t seg = act & ~lng & from & upto;
-          if (seg) {
-            // consecutive short runs flattened into full 32-lane chunks
-            const int m = __popc(seg);
-            const int src = lane < m ? int(__fns(seg, 0, lane + 1)) : 0;
-            const int32_t n_c = __shfl_sync(FULL, n, src);
-            const uint32_t lo_c = __shfl_sync(FULL, lo, src), b32_c = __shfl_sync(FULL, b32, src);
-            const float w_c = __shfl_sync(FULL, w0, src), s_c = __shfl_sync(FULL, scale, src);
-            const int32_t sz = lane < m ? n_c : 0;
-            int32_t incl = sz;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-              const int32_t y = __shfl_up_sync(FULL, incl, o);
-              if (lane >= o) incl += y;
-            }
-            const int32_t P = incl - sz;
-            const int32_t total = __shfl_sync(FULL, incl, 31);
-            for (int32_t F = 0; F < total; F += 32) {
-              const int32_t f = F + lane;
-              const bool valid = f < total;
-              const uint32_t bit = (lane < m && P >= F && P < F + 32) ? (1u << (P - F)) : 0u;
-              const uint32_t S = __reduce_or_sync(FULL, bit);
-              const int jF = __popc(__ballot_sync(FULL, lane < m && P <= F)) - 1;
-              int j = jF + __popc(S & (lanemask_lt() | (1u << lane)) & ~1u);
-              j = valid ? j : 0;
-              const int32_t Pj = __shfl_sync(FULL, P, j);
-              const uint32_t loj = __shfl_sync(FULL, lo_c, j), bj = __shfl_sync(FULL, b32_c, j);
-              const float wj = __shfl_sync(FULL, w_c, j), sj = __shfl_sync(FULL, s_c, j);
-              int32_t col = -1;
-              float wv = 0.f;
-              if (valid) {
-                const int64_t pos = (int64_t(bj) << 5) + loj + (f - Pj);
-                col = __ldg(doc_ids + pos) - d0i;
-                wv = WDecode<WT>::get(wts, pos, sj);
-              }
-              // lanes on the same document (different terms) apply in term (= lane) order
-              const int32_t dkey = (valid && uint32_t(col) < span) ? col : -1 - lane;
-              const uint32_t peers = __match_any_sync(FULL, dkey);
-              const int rank = __popc(peers & lanemask_lt());
-              const int top = int(__reduce_max_sync(FULL, uint32_t(rank)));
-              for (int rr = 0; rr <= top; ++rr) {
-                if (rank == rr) acc_add(acc, col, span, wj, wv);
-                __syncwarp();
-              }
-            }
-          }
-          if (next_long >= 32) break;
-          // one long (or multi-entry) run
-          const int jl = next_long;
-          const int32_t nl_n = __shfl_sync(FULL, n, jl);
-          const uint32_t lo_l = __shfl_sync(FULL, lo, jl), b32_l = __shfl_sync(FULL, b32, jl);
-          const int32_t e0_l = __shfl_sync(FULL, e0, jl), ne_l = __shfl_sync(FULL, ne, jl);
-          const float w0_l = __shfl_sync(FULL, w0, jl), sc_l = __shfl_sync(FULL, scale, jl);
-          const int64_t base = (int64_t(b32_l) << 5) + lo_l;
-          if (ne_l == 1 && nl_n <= 64) {
-            // the next run, if it is long with one entry and nothing lies between: as a pair
-            const uint32_t after = act & ~((2u << jl) - 1u);
-            const int j2 = after ? __ffs(after) - 1 : 32;
-            if (j2 < 32 && ((lng >> j2) & 1u)) {
-              const int32_t n2 = __shfl_sync(FULL, n, j2), ne2 = __shfl_sync(FULL, ne, j2);
-              const uint32_t lo2 = __shfl_sync(FULL, lo, j2), b322 = __shfl_sync(FULL, b32, j2);
-              const float w02 = __shfl_sync(FULL, w0, j2), sc2 = __shfl_sync(FULL, scale, j2);
-              if (ne2 == 1 && n2 <= 64) {
-                const int64_t base2 = (int64_t(b322) << 5) + lo2;
-                run_pair<WT>(doc_ids + base, wts + base, sc_l, nl_n, w0_l, doc_ids + base2, wts + base2, sc2, n2,
-                             w02, d0i, span, acc);
-                c = j2 + 1;
-                continue;
-              }
-            }
-          }
-          if (ne_l == 1) {
-            run_window<WT, 1>(doc_ids + base, wts + base, sc_l, nl_n, d0i, span, acc, w0_l, 0.f, nullptr, 0);
-          } else if (ne_l == 2) {
-            run_window<WT, 2>(doc_ids + base, wts + base, sc_l, nl_n, d0i, span, acc, w0_l, ent_w[e0_l + 1],
-                              nullptr, 0);
-          } else {
-            run_window<WT, 0>(doc_ids + base, wts + base, sc_l, nl_n, d0i, span, acc, 0.f, 0.f, ent_w + e0_l,
-                              ne_l);
-          }
-          c = jl + 1;
-        }
-      }
-      __syncwarp();
-
-      // 3. fused selection: the documents whose score reaches the query's threshold go to
-      // its candidate buffer (a superset of the keys >= threshold is harmless: only the k
-      // largest survive the compactions and the merge)
-      uint64_t thr = uint64_t(g_pub);
-      if (p.n_shards > 1) {
-#pragma unroll
-        for (int o = 16; o; o >>= 1) bnd = min(bnd, __shfl_xor_sync(FULL, bnd, o));
-        thr = max(thr, uint64_t(bnd));
-      }
-      if constexpr (kMode == kModeTree) {
-        // small-batch mode (one selection pass per tile): the tile's own exact top-k
-        tile_topk(acc, span, uint32_t(p.doc_base + d0i), min(p.tile_k, int32_t(span)), p.tile_k, hist,
-                  p.tile_out + (int64_t(q) * p.n_blocks + b) * p.tile_k);
-        continue;
-      }
-      if constexpr (kMode == kModeDense) {
-        // every document's key (lane writes columns 128 i + 4 lane .. + 3, two 16-byte stores)
-        uint64_t* __restrict__ row = p.dense + int64_t(q - p.q_lo) * p.dense_ld + d0i;
-        const uint32_t dbase = uint32_t(p.doc_base + d0i);
-#pragma unroll
-        for (int i = 0; i < kTile / 128; ++i) {
-          const uint32_t c = uint32_t(128 * i + 4 * lane);
-          const float4 v = *reinterpret_cast<const float4*>(acc + c);
-          ulonglong2 k0, k1;
-          k0.x = c + 0 < span ? pack_key(v.x, dbase + c + 0) : 0ull;
-          k0.y = c + 1 < span ? pack_key(v.y, dbase + c + 1) : 0ull;
-          k1.x = c + 2 < span ? pack_key(v.z, dbase + c + 2) : 0ull;
-          k1.y = c + 3 < span ? pack_key(v.w, dbase + c + 3) : 0ull;
-          *reinterpret_cast<ulonglong2*>(row + c) = k0;
-          *reinterpret_cast<ulonglong2*>(row + c + 2) = k1;
-        }
-        continue;
-      }
-#pragma unroll
-      for (int h = 0; h < kTile / kSel; ++h) {
-        if (uint32_t(h * kSel) >= span) break;
-        const uint32_t sp = min(span - uint32_t(h * kSel), uint32_t(kSel));
-        const uint32_t m = mark_tile(acc + h * kSel, lane, sp, thr);
-        if (__any_sync(FULL, m != 0u)) {
-          QueryBuf qb{p.cand + int64_t(q) * 3 * p.cand_stride, p.cand_stride, p.gthr + q, p.rg + q,
-                      p.done + 2 * q, p.cdone + q, p.fault, p.cap, p.k, p.wait_limit, p.kg};
-          const uint64_t pub =
-              append_candidates(qb, acc + h * kSel, sp, uint32_t(p.doc_base + d0i + h * kSel), hist, thr, m);
-          // this shard's row of every board: local, then the peers' (remote reductions over
-          // NVLink; nothing waits on them)
-          if (pub != 0ull) {
-            const int64_t slot = int64_t(p.shard) * p.B + q;
-            if (lane == 0) atomicMax(p.board + slot, (unsigned long long)pub);
-#pragma unroll
-            for (int r = 0; r < kMaxPeers; ++r) {
-              if (r < p.n_peers && lane == r + 1) atomicMax(p.peer_thr[r] + slot, (unsigned long long)pub);
-            }
-          }
-        }
-      }
+      item_tail_select<WT, kMode>(p, q, b, acc, hist);
     }
   }
 }
 
+#include "score_tc.cuh"
+
 struct Cfg {
   bool tree = false;   // small-batch mode: per-tile top-k lists and a merge tree
   bool dense = false;  // k above kMaxSmemK: all keys written, a window of queries at a time
+  bool tc = false;     // head terms on the tensor cores (score_tc_kernel)
+  int64_t qh_rows = 0, off_qh = 0, off_qhlo = 0;
   int64_t dense_q = 0, dense_ld = 0, off_dense = 0, off_large = 0;
   int64_t off_tiles = 0, off_lv0 = 0, off_lv1 = 0;
   int npow2 = 0, cap = 0, smem = 0, ctas_per_sm = 0, grid = 0;
@@ -1058,6 +1075,24 @@ struct Cfg {
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 std::atomic<int32_t> g_wait_limit{kSpinLimit};
+// How head terms are summed.  The automatic mode uses the CUDA cores: for the fp32 head rows
+// of fp32 and uint8 indexes the tensor-core path measured slower on B200 (see score_tc.cuh),
+// and bf16 rows have no tensor-core path.
+std::atomic<int32_t> g_head_mode{GSP_HEAD_AUTO};
+
+PFN_cuTensorMapEncodeTiled_v12000 tma_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      (void)cudaGetLastError();
+      f = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
 // largest per-tile list buffer (B x tiles x k keys) for which a batch takes the merge tree
 std::atomic<int64_t> g_tree_limit{int64_t(256) << 20};
 int64_t align8(int64_t x) { return (x + 7) / 8 * 8; }
@@ -1081,7 +1116,12 @@ void set_layout(Cfg& c, int64_t B) {
   c.off_counts = o; o = align256(o + B * 3 * 4);
   // cleared by every call: thresholds [B] u64, reservation words [B] u64, written
   // counters [B, 2], finished compactions [B], item counter u64, fault flag
-  c.off_zero = o; c.zero_bytes = align8(2 * B * 8 + 3 * B * 4) + 16; o = align256(o + c.zero_bytes);
+  c.off_zero = o; c.zero_bytes = align8(2 * B * 8 + 3 * B * 4) + 24; o = align256(o + c.zero_bytes);
+  if (c.tc) {
+    c.qh_rows = (B + tc::kUnitQ - 1) / tc::kUnitQ * tc::kUnitQ;
+    c.off_qh = o; o = align256(o + c.qh_rows * 128 * 4);
+    c.off_qhlo = o; o = align256(o + c.qh_rows * 128 * 4);
+  }
   if (c.tree) {
     const int64_t g1 = (c.n_blocks + kTreeFanIn - 1) / kTreeFanIn;
     c.off_tiles = o; o = align256(o + B * c.n_blocks * c.kk * 8);
@@ -1136,6 +1176,12 @@ int make_cfg(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k, Cfg& c) 
   // apply: every key is written out for a window of queries whose keys (and the global
   // sort's two buffers) fit about kDenseBytes, and the windows are selected one by one.
   c.dense = c.kk > kMaxSmemK;
+  // head terms on the tensor cores: fp32 head rows (fp32 and uint8 indexes) with their 3xTF32
+  // low parts, unless the caller asked for the canonical CUDA-core order
+  const int32_t mode = g_head_mode.load();
+  c.tc = mode == GSP_HEAD_TENSOR_CORES && B > 0 && c.n_blocks > 0 && ix->n_head >= tc::kKC &&
+         ix->n_head <= 128 && ix->head_lo != nullptr && ix->head_wdtype == GSP_W_F32 &&
+         tma_encoder() != nullptr;
   if (c.dense) {
     c.dense_ld = c.n_blocks * kTile;
     const int64_t per_q = c.dense_ld * 8 + large_k_ws_bytes(1, c.kk);
@@ -1160,29 +1206,94 @@ Profile& profile() {
   return p;
 }
 
+// The profiling event pair of the next scoring launch, or null when profiling is off.
+int profile_slot(std::pair<cudaEvent_t, cudaEvent_t>** evp) {
+  Profile& pr = profile();
+  *evp = nullptr;
+  std::lock_guard<std::mutex> g(pr.mu);
+  if (pr.on) {
+    if (pr.used == pr.ev.size()) {
+      cudaEvent_t a, b;
+      GSP_CUDA(cudaEventCreate(&a));
+      GSP_CUDA(cudaEventCreate(&b));
+      pr.ev.emplace_back(a, b);
+    }
+    *evp = &pr.ev[pr.used++];
+  }
+  return GSP_OK;
+}
+
 template <typename WT, typename HT>
 int launch_score(const ScoreParams& p, const Cfg& c, cudaStream_t st) {
   auto kern = c.dense ? score_kernel<WT, HT, kModeDense>
                       : (c.tree ? score_kernel<WT, HT, kModeTree> : score_kernel<WT, HT, kModeBuffers>);
   if (int rc = ensure_smem(reinterpret_cast<const void*>(kern), c.smem)) return rc;
-  Profile& pr = profile();
   std::pair<cudaEvent_t, cudaEvent_t>* evp = nullptr;
-  {
-    std::lock_guard<std::mutex> g(pr.mu);
-    if (pr.on) {
-      if (pr.used == pr.ev.size()) {
-        cudaEvent_t a, b;
-        GSP_CUDA(cudaEventCreate(&a));
-        GSP_CUDA(cudaEventCreate(&b));
-        pr.ev.emplace_back(a, b);
-      }
-      evp = &pr.ev[pr.used++];
-    }
-  }
+  if (int rc = profile_slot(&evp)) return rc;
   if (evp) GSP_CUDA(cudaEventRecord(evp->first, st));
   kern<<<unsigned(c.grid), kWarps * 32, c.smem, st>>>(p);
   GSP_CHECK_LAUNCH();
   if (evp) GSP_CUDA(cudaEventRecord(evp->second, st));
+  return GSP_OK;
+}
+
+// The tensor-core scorer over queries [p.q_lo, p.q_lo + p.q_n): one persistent CTA per SM.
+template <typename WT>
+int launch_score_tc(const ScoreParams& p, TcParams& tp, const Cfg& c, cudaStream_t st) {
+  auto kern = c.dense ? score_tc_kernel<WT, kModeDense>
+                      : (c.tree ? score_tc_kernel<WT, kModeTree> : score_tc_kernel<WT, kModeBuffers>);
+  const int smem = tc::kSmem + 1024;
+  if (int rc = ensure_smem(reinterpret_cast<const void*>(kern), smem)) return rc;
+  tp.n_groups = (p.q_n + tc::kUnitQ - 1) / tc::kUnitQ;
+  tp.n_units = int32_t(c.n_blocks) * tp.n_groups;
+  GSP_CUDA(cudaMemsetAsync(tp.unit_next, 0, sizeof(unsigned long long), st));
+  std::pair<cudaEvent_t, cudaEvent_t>* evp = nullptr;
+  if (int rc = profile_slot(&evp)) return rc;
+  if (evp) GSP_CUDA(cudaEventRecord(evp->first, st));
+  const int grid = std::max(1, std::min(num_sms(), tp.n_units));
+  kern<<<unsigned(grid), tc::kThreads, smem, st>>>(p, tp);
+  GSP_CHECK_LAUNCH();
+  if (evp) GSP_CUDA(cudaEventRecord(evp->second, st));
+  return GSP_OK;
+}
+
+// Tensor maps of the head rows (hi = the rows, lo = their 3xTF32 low parts) and of the
+// batch's dense query head weights.
+int make_tc_params(const gsp_index_view* ix, const Cfg& c, float* qh, float* qh_lo, TcParams& tp) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tma_encoder();
+  GSP_REQUIRE(enc, GSP_ERR_CUDA, "score: cuTensorMapEncodeTiled is not available");
+  GSP_REQUIRE(ix->head_ld % 32 == 0 && (reinterpret_cast<uintptr_t>(ix->head_rows) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(ix->head_lo) & 15) == 0,
+              GSP_ERR_ARG, "score: head rows must be 16-byte aligned with a multiple of 32 columns");
+  {
+    const cuuint64_t dims[3] = {32, cuuint64_t(ix->n_head), cuuint64_t(ix->head_ld / 32)};
+    const cuuint64_t strides[2] = {cuuint64_t(ix->head_ld) * 4, 128};
+    const cuuint32_t box[3] = {32, tc::kKC, 4};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const void* src[2] = {ix->head_rows, ix->head_lo};
+    CUtensorMap* dst[2] = {&tp.a_hi, &tp.a_lo};
+    for (int i = 0; i < 2; ++i) {
+      const CUresult r = enc(dst[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(src[i]), dims, strides, box,
+                             es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      GSP_REQUIRE(r == CUDA_SUCCESS, GSP_ERR_CUDA, "score: head-row tensor map failed (%d)", int(r));
+    }
+  }
+  {
+    const cuuint64_t dims[2] = {128, cuuint64_t(c.qh_rows)};
+    const cuuint64_t strides[1] = {128 * 4};
+    const cuuint32_t box[2] = {tc::kKC, tc::kUnitQ};
+    const cuuint32_t es[2] = {1, 1};
+    float* src[2] = {qh, qh_lo};
+    CUtensorMap* dst[2] = {&tp.b_hi, &tp.b_lo};
+    for (int i = 0; i < 2; ++i) {
+      const CUresult r = enc(dst[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, src[i], dims, strides, box, es,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      GSP_REQUIRE(r == CUDA_SUCCESS, GSP_ERR_CUDA, "score: query-weight tensor map failed (%d)", int(r));
+    }
+  }
+  tp.n_kc = (ix->n_head + tc::kKC - 1) / tc::kKC;
   return GSP_OK;
 }
 
@@ -1251,6 +1362,7 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.counts = reinterpret_cast<int32_t*>(w + c.off_counts);
   p.item_next = reinterpret_cast<unsigned long long*>(z + align8(2 * B * 8 + 3 * B * 4));
   p.fault = reinterpret_cast<int32_t*>(p.item_next + 1);
+  unsigned long long* unit_next = p.item_next + 2;
   GSP_REQUIRE(n_shards >= 1 && n_shards <= kMaxPeers + 1 && shard >= 0 && shard < n_shards &&
                   (n_shards == 1 || (board && peers)),
               GSP_ERR_ARG, "gsp_score_topk_shared: bad shard arguments (shard %d of %d, at most %d)", shard,
@@ -1284,7 +1396,21 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   const int32_t hdt = ix->n_head > 0 ? ix->head_wdtype : ix->wdtype;
   GSP_REQUIRE(hdt == ix->wdtype || (ix->wdtype == GSP_W_U8 && hdt == GSP_W_F32), GSP_ERR_ARG,
               "gsp_score_topk: head rows of type %d do not go with weights of type %d", hdt, ix->wdtype);
+  TcParams tp;
+  if (c.tc) {
+    float* qh = reinterpret_cast<float*>(w + c.off_qh);
+    float* qh_lo = reinterpret_cast<float*>(w + c.off_qhlo);
+    qhead_kernel<<<unsigned(c.qh_rows), 128, 0, st>>>(p, int32_t(B), ix->n_head, qh, qh_lo);
+    GSP_CHECK_LAUNCH();
+    rc = make_tc_params(ix, c, qh, qh_lo, tp);
+    if (rc) return rc;
+    tp.unit_next = unit_next;
+  }
   auto launch = [&](const ScoreParams& pp) -> int {
+    if (c.tc) {
+      // fp32 head rows: fp32 postings, or uint8 postings with dequantised rows
+      return ix->wdtype == GSP_W_U8 ? launch_score_tc<uint8_t>(pp, tp, c, st) : launch_score_tc<float>(pp, tp, c, st);
+    }
     switch (ix->wdtype) {
       case GSP_W_F32: return launch_score<float, float>(pp, c, st);
       case GSP_W_BF16: return launch_score<__nv_bfloat16, __nv_bfloat16>(pp, c, st);
@@ -1347,6 +1473,15 @@ extern "C" int gsp_set_wait_limit(int32_t polls) {
 }
 
 extern "C" int32_t gsp_get_wait_limit(void) { return g_wait_limit.load(); }
+
+extern "C" int gsp_set_head_mode(int32_t mode) {
+  GSP_REQUIRE(mode == GSP_HEAD_AUTO || mode == GSP_HEAD_CUDA_CORES || mode == GSP_HEAD_TENSOR_CORES, GSP_ERR_ARG,
+              "gsp_set_head_mode: unknown mode %d", mode);
+  g_head_mode.store(mode);
+  return GSP_OK;
+}
+
+extern "C" int32_t gsp_get_head_mode(void) { return g_head_mode.load(); }
 
 extern "C" int gsp_set_tree_limit(int64_t bytes) {
   GSP_REQUIRE(bytes >= 0, GSP_ERR_ARG, "gsp_set_tree_limit: negative limit");

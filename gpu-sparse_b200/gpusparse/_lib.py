@@ -25,6 +25,7 @@ GSP_ERR_UNSUPPORTED = 6
 GSP_ERR_BLOCK_PL = 7
 
 W_F32, W_BF16, W_U8 = 0, 1, 2
+HEAD_AUTO, HEAD_CUDA_CORES, HEAD_TENSOR_CORES = 0, 1, 2   # gsp_set_head_mode
 CHECK_WS_BYTES = 16     # GSP_CHECK_WS_BYTES
 
 # every symbol include/gpusparse.h declares
@@ -33,7 +34,8 @@ EXPORTS = (
     "gsp_synth_fill", "gsp_index_ws_bytes", "gsp_index_count", "gsp_index_fill",
     "gsp_index_count_chunk", "gsp_index_count_finish", "gsp_index_fill_chunk",
     "gsp_index_fill_finish", "gsp_csr_dedup_count", "gsp_csr_dedup_fill",
-    "gsp_index_quantize", "gsp_index_head_rows", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
+    "gsp_index_quantize", "gsp_index_head_rows", "gsp_index_head_lo", "gsp_set_head_mode",
+    "gsp_get_head_mode", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
     "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_score_topk_shared", "gsp_board_alloc",
     "gsp_board_free", "gsp_board_open", "gsp_board_close", "gsp_board_clear", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_set_tree_limit", "gsp_get_tree_limit", "gsp_merge_ws_bytes", "gsp_merge_topk",
     "gsp_compacted_ws_bytes", "gsp_compacted_topk",
@@ -49,7 +51,7 @@ class IndexView(ctypes.Structure):
         ("term_scale", ctypes.c_void_p), ("offsets", ctypes.c_void_p),
         ("lengths", ctypes.c_void_p), ("block_starts", ctypes.c_void_p),
         ("n_head", ctypes.c_int32), ("head_wdtype", ctypes.c_int32), ("head_slot", ctypes.c_void_p),
-        ("head_rows", ctypes.c_void_p), ("head_ld", ctypes.c_int64),
+        ("head_rows", ctypes.c_void_p), ("head_ld", ctypes.c_int64), ("head_lo", ctypes.c_void_p),
     ]
 
 
@@ -98,6 +100,9 @@ def lib() -> ctypes.CDLL:
             "gsp_csr_dedup_fill": (ctypes.c_int, [i64, p, p, p, p, p, p, p]),
             "gsp_index_quantize": (ctypes.c_int, [i32, i64, p, p, p, p, i32, p, p, p]),
             "gsp_index_head_rows": (ctypes.c_int, [i32, p, p, p, p, p, i32, i64, p, p]),
+            "gsp_index_head_lo": (ctypes.c_int, [i64, p, p, p]),
+            "gsp_set_head_mode": (ctypes.c_int, [i32]),
+            "gsp_get_head_mode": (i32, []),
             "gsp_check_sorted": (ctypes.c_int, [i32, p, p, p, ctypes.POINTER(i64),
                                                 ctypes.POINTER(i64), p, i64, p]),
             "gsp_chunk_bounds": (ctypes.c_int, [i64, i32, i64, p, p, p, p, p, i64, p]),

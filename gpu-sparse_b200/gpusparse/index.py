@@ -12,8 +12,9 @@ keeps:
 * ``doc_base``: global id of local document 0 when the index is one doc-range shard;
 * ``head_ids`` / ``head_slot`` / ``head_rows``: the N_HEAD terms with the longest posting
   lists, also stored as dense rows [n_head, ld] (the weight of the term in every document,
-  0 where absent) that the scorer streams with coalesced vector loads into register
-  accumulators instead of scattering their postings.
+  0 where absent) that the scorer sums as one dense product per tile instead of scattering
+  their postings; ``head_lo`` (fp32 rows only) holds each element minus its tf32
+  truncation, so that the tensor cores carry the full fp32 value (3xTF32).
 
 Builders run on the GPU (csrc/build.cu); the CSR is only copied host -> device, in chunks
 of rows when it comes from the host (``build_from_host_csr``, ``build_streamed``).
@@ -59,6 +60,7 @@ class GPUInvertedIndex:
     head_rows: Optional[torch.Tensor] = None
     head_ld: int = 0
     head_wdtype: int = 0          # dtype code of head_rows (fp32 rows for uint8 postings)
+    head_lo: Optional[torch.Tensor] = None   # fp32 rows: low tf32 parts for the tensor cores
     _view: object = field(default=None, repr=False, compare=False)
 
 
@@ -244,6 +246,7 @@ def quantize_(index: GPUInvertedIndex, weight_dtype: str, keep_fp32: bool = True
     if not keep_fp32:
         index.scores = None
     index.head_rows = None          # rebuilt in the new weight dtype on next use
+    index.head_lo = None
     index._view = None
 
 
@@ -323,8 +326,14 @@ def ensure_head(index: GPUInvertedIndex, n_head: int = N_HEAD, head_ids=None) ->
         L.check(L.lib().gsp_index_head_rows(H, L.ptr(ids), L.ptr(index.offsets), L.ptr(lengths),
                                             L.ptr(index.doc_ids), L.ptr(w), code, ld, L.ptr(rows),
                                             L.stream_of(dev)), "head rows")
+        lo = None
+        if code == L.W_F32 and H > 0:
+            lo = torch.empty_like(rows)
+            L.check(L.lib().gsp_index_head_lo(rows.numel(), L.ptr(rows), L.ptr(lo), L.stream_of(dev)),
+                    "head rows")
     index.head_ids, index.head_slot, index.head_rows, index.head_ld = ids, slot, rows, ld
     index.head_wdtype = code
+    index.head_lo = lo
 
 
 # ------------------------------------------------------------------ persistence
@@ -332,7 +341,7 @@ def ensure_head(index: GPUInvertedIndex, n_head: int = N_HEAD, head_ids=None) ->
 # arrays, block rows and head rows) can be written once and loaded straight to a device.
 _FORMAT = "gpusparse-index-v1"
 _ARRAYS = ("doc_ids", "scores", "offsets", "lengths", "padded_lengths", "max_scores", "weights_q",
-           "term_scale", "block_starts", "head_ids", "head_slot", "head_rows")
+           "term_scale", "block_starts", "head_ids", "head_slot", "head_rows", "head_lo")
 _SCALARS = ("num_docs", "vocab_size", "weight_dtype", "block_docs", "doc_base", "head_ld",
             "head_wdtype")
 
@@ -362,7 +371,7 @@ def load_index(path, device) -> GPUInvertedIndex:
                            vocab_size=state["vocab_size"], device=device,
                            weight_dtype=state["weight_dtype"], block_docs=state["block_docs"],
                            doc_base=state["doc_base"])
-    for f in ("weights_q", "term_scale", "block_starts", "head_ids", "head_slot", "head_rows"):
+    for f in ("weights_q", "term_scale", "block_starts", "head_ids", "head_slot", "head_rows", "head_lo"):
         setattr(idx, f, arr.get(f))
     idx.head_ld = state["head_ld"]
     idx.head_wdtype = state["head_wdtype"]
@@ -397,6 +406,8 @@ def view(index: GPUInvertedIndex) -> L.IndexView:
     v.head_rows = index.head_rows.data_ptr()
     v.head_ld = int(index.head_ld)
     v.head_wdtype = int(getattr(index, "head_wdtype", code))
+    lo = getattr(index, "head_lo", None)
+    v.head_lo = lo.data_ptr() if lo is not None else 0
     return v
 
 
@@ -472,7 +483,7 @@ def index_memory_stats(index: GPUInvertedIndex) -> dict:
     scores_bytes = nbytes(index.scores) + nbytes(index.weights_q) + nbytes(index.term_scale)
     meta_bytes = (nbytes(index.offsets) + nbytes(index.lengths) + nbytes(index.padded_lengths)
                   + nbytes(index.max_scores) + nbytes(index.block_starts)
-                  + nbytes(getattr(index, "head_rows", None)))
+                  + nbytes(getattr(index, "head_rows", None)) + nbytes(getattr(index, "head_lo", None)))
     n = int(index.lengths.sum().item())
     npad = int(index.padded_lengths.sum().item()) if index.padded_lengths is not None else n
     return {"doc_ids_MB": doc_ids_bytes / 1e6, "scores_MB": scores_bytes / 1e6,

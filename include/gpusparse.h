@@ -146,6 +146,11 @@ int gsp_index_quantize(int32_t V, int64_t total_padded, const int64_t* offsets,
 int gsp_index_head_rows(int32_t H, const int32_t* head_ids, const int64_t* offsets,
                         const int32_t* lengths, const int32_t* doc_ids, const void* weights,
                         int32_t wdtype, int64_t ld, void* rows, void* stream);
+/* lo[i] = rows[i] - trunc_tf32(rows[i]) for n fp32 values (no reference counterpart): the
+ * low parts of the dense head rows for the tensor-core head phase (gsp_index_view.head_lo).
+ * The tensor core reads an fp32 operand as tf32 by ignoring its low 13 mantissa bits, so
+ * rows + lo carry the full fp32 value through a 3xTF32 product. */
+int gsp_index_head_lo(int64_t n, const float* rows, float* lo, void* stream);
 /* Counts posting lists that are not ascending in doc id (*n_bad) and, when n_dup is not
  * NULL, lists that repeat a doc id (*n_dup); both written on the host (this call
  * synchronises the stream).  ws: at least GSP_CHECK_WS_BYTES of device scratch.  The
@@ -187,7 +192,32 @@ typedef struct gsp_index_view {
     const int32_t* head_slot;  /* [V]: row of term t in head_rows, or -1 */
     const void* head_rows;     /* [n_head, head_ld], head_wdtype */
     int64_t head_ld;
+    /* fp32 head rows only, optional: head_rows[i] - (head_rows[i] with its low 13 mantissa
+       bits cleared), the second tf32 term of each element for the tensor-core head phase
+       (gsp_index_head_lo); NULL keeps the head terms on the CUDA cores */
+    const float* head_lo;
 } gsp_index_view;
+
+/* How the head terms (those with dense rows) are summed (no reference counterpart):
+ *   GSP_HEAD_AUTO          the library's choice, currently GSP_HEAD_CUDA_CORES for every
+ *                          index (the default): on B200 the tensor-core path measured slower
+ *                          for fp32 head rows (48.9 against 35.1 ms per batch at 8.8M
+ *                          documents, 1000 queries, k = 1000), its operand stream being
+ *                          limited by TMA throughput
+ *   GSP_HEAD_CUDA_CORES    acc = fma(q_w, d_w, acc) in the canonical order: results bitwise
+ *                          equal to the CPU oracle's
+ *   GSP_HEAD_TENSOR_CORES  tcgen05 MMAs (tf32, operands split 3xTF32: fp32 accuracy to about
+ *                          1e-6 relative) for indexes with fp32 head rows and head_lo, any
+ *                          batch size; other indexes keep the CUDA cores.  A query's weights
+ *                          for a repeated head term are added before the product; the tail
+ *                          terms then follow in the canonical order, and results are bitwise
+ *                          reproducible run to run.
+ * Applies to calls issued after it; process-wide. */
+#define GSP_HEAD_AUTO 0
+#define GSP_HEAD_CUDA_CORES 1
+#define GSP_HEAD_TENSOR_CORES 2
+int gsp_set_head_mode(int32_t mode);
+int32_t gsp_get_head_mode(void);
 
 /* Workspace bytes for gsp_score_topk with this batch shape (a negative status on error). */
 int64_t gsp_score_ws_bytes(const gsp_index_view* ix, int64_t B, int64_t W, int64_t k);

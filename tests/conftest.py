@@ -10,6 +10,8 @@ for p in (ROOT, os.path.join(ROOT, "gpu-sparse_b200"), os.path.join(ROOT, "tests
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
     config.addinivalue_line("markers", "slow: full-size configuration")
+    config.addinivalue_line("markers", "tensorcore: runs the head terms on the tensor cores "
+                                       "(checked within the 1e-5 tolerance, not bit for bit)")
 
 
 import pytest  # noqa: E402
@@ -28,3 +30,22 @@ def shared_buffers_only():
         yield
     finally:
         lib.gsp_set_tree_limit(default)
+
+
+@pytest.fixture(autouse=True)
+def head_mode(request):
+    """Bit-exact tests run the head terms in the canonical CUDA-core order (the oracle's);
+    tests marked ``tensorcore`` force the tensor-core head phase.  The library's default
+    (automatic) mode is restored afterwards."""
+    try:
+        import gpusparse._lib as L
+        lib = L.lib()
+    except Exception:          # no library: nothing to set (CPU-only checks)
+        yield
+        return
+    mode = L.HEAD_TENSOR_CORES if request.node.get_closest_marker("tensorcore") else L.HEAD_CUDA_CORES
+    L.check(lib.gsp_set_head_mode(mode), "head mode")
+    try:
+        yield
+    finally:
+        lib.gsp_set_head_mode(L.HEAD_AUTO)

@@ -108,7 +108,9 @@ def test_duplicate_terms_in_a_document_are_merged():
     ref = O.build_index_reference(m, 8)
     assert np.array_equal(idx.doc_ids.cpu().numpy(), ref.doc_ids)
     assert np.array_equal(idx.scores.cpu().numpy(), ref.scores)
-    assert float(idx.scores.cpu().numpy()[0]) == 0.75         # doc 0, term 4: 0.5 + 0.25
+    o4 = int(idx.offsets.cpu().numpy()[4])                    # term 4: docs 0 and 1
+    assert idx.doc_ids.cpu().numpy()[o4] == 0
+    assert float(idx.scores.cpu().numpy()[o4]) == 0.75        # doc 0: 0.5 + 0.25
 
 
 def test_bad_column_id_raises():
