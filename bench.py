@@ -98,6 +98,38 @@ def workload(args):
     return c
 
 
+def source_tag():
+    """Short hash of the CUDA sources (csrc/*.cu, *.cuh): ties a committed ncu figure to the
+    kernels it was measured on."""
+    import hashlib
+    d = os.path.join(ROOT, "gpu-sparse_b200", "csrc")
+    h = hashlib.sha256()
+    for f in sorted(os.listdir(d)):
+        if f.endswith((".cu", ".cuh")):
+            h.update(f.encode())
+            h.update(open(os.path.join(d, f), "rb").read())
+    return h.hexdigest()[:12]
+
+
+def measured_traffic(config, world, num_docs_override):
+    """DRAM bytes per scoring launch from the committed ncu summary
+    (profiles/score_kernel_traffic_config<c>.md), used only when its source tag matches the
+    sources being benchmarked; otherwise None and the reason."""
+    import re
+    tp = os.path.join(ROOT, "profiles", f"score_kernel_traffic_config{config}.md")
+    if num_docs_override:
+        return None, "no committed profile for a --num-docs override"
+    if not os.path.exists(tp):
+        return None, f"no committed profile for config {config}"
+    txt = open(tp).read()
+    m = re.search(rf"config{config}_gpus{world} dram_bytes_per_launch: (\d+) source: (\w+)", txt)
+    if not m:
+        return None, f"the committed profile has no figure for config {config} on {world} GPU(s)"
+    if m.group(2) != source_tag():
+        return None, f"the committed profile measured sources {m.group(2)}, these are {source_tag()}"
+    return int(m.group(1)), f"ncu, sources {m.group(2)} ({os.path.relpath(tp, ROOT)})"
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -220,6 +252,80 @@ def cpu_sample(index, qi, qs, k, gpu_s, gpu_i, target_s):
             "wall_s": round(wall, 3), "cpu_s": round(cpu, 3),
             "cpu_over_wall": round(cpu / wall, 2), "parity_bit_exact_vs_gpu": exact,
             "single_core": {"value": n1 / wall1, "unit": "queries/s", "sample": f"{n1} queries"}}
+
+
+def physical_cores():
+    """One logical CPU per physical core (lscpu), within this process's affinity mask; the
+    reference notes that nproc can misreport (final_results/corrected_2026_08/README.md)."""
+    allowed = sorted(os.sched_getaffinity(0))
+    try:
+        out = subprocess.run(["lscpu", "-p=CPU,CORE,SOCKET"], capture_output=True, text=True,
+                             timeout=20).stdout
+        first = {}
+        for line in out.splitlines():
+            if line.startswith("#"):
+                continue
+            cpu, core, sock = (int(x) for x in line.split(",")[:3])
+            if cpu in allowed:
+                first.setdefault((sock, core), cpu)
+        cpus = sorted(first.values())
+        return cpus or allowed, "lscpu"
+    except Exception:
+        return allowed, "affinity mask"
+
+
+def reference_cpu_paths(wl, qi_h, qs_h, k, target_s):
+    """The reference's own CPU scoring paths on a bounded sample, pinned with
+    sched_setaffinity (the taskset of baselines/seismic_k_calibration.py:50-52) to all
+    physical cores and to one core: the exhaustive dense fp32 path
+    (src/remeasure_2026_09.py:238-258: densified document chunks, Q @ D^T, torch.topk
+    merge) and cpu_sequential_score (src/gpu_scoring.py:221-259, pure Python).  Each
+    covers a prefix of the corpus's documents and is scaled to whole-corpus queries/s
+    (both cost time in proportion to the documents scored)."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    N = wl["num_docs"]
+    dlaw = O.Law(zipf_s=wl["zipf_s"])
+    cores, how = physical_cores()
+    saved_mask, saved_threads = os.sched_getaffinity(0), torch.get_num_threads()
+    res = {}
+    try:
+        # dense: a few chunks of documents, as many queries as make ~target_s of work
+        nd = min(N, 4 * 16384)
+        ip, ix, dt = O.synth_csr(nd, V, seed=0, law=dlaw)
+        for label, cpu_set in (("all_cores", cores), ("one_core", cores[:1])):
+            os.sched_setaffinity(0, cpu_set)
+            torch.set_num_threads(len(cpu_set))
+            nq = 8 if label == "one_core" else 32
+            Q = O.dense_query_matrix(qi_h[:nq], qs_h[:nq], V)
+            r0 = resource.getrusage(resource.RUSAGE_SELF)
+            t0 = time.perf_counter()
+            O.dense_reference_topk(ip, ix, dt, V, Q, k, doc_hi=nd)
+            wall = time.perf_counter() - t0
+            r1 = resource.getrusage(resource.RUSAGE_SELF)
+            cpu = (r1.ru_utime - r0.ru_utime) + (r1.ru_stime - r0.ru_stime)
+            res[f"dense_{label}"] = {
+                "value": nq / (wall * N / nd), "unit": "queries/s", "cores": len(cpu_set),
+                "pin": f"{how}: cpus {cpu_set[0]}..{cpu_set[-1]}" if len(cpu_set) > 1 else f"cpu {cpu_set[0]}",
+                "sample": f"{nq} queries x the first {nd:,} docs, scaled to {N:,}",
+                "wall_s": round(wall, 3), "cpu_s": round(cpu, 3), "cpu_over_wall": round(cpu / wall, 2)}
+        del ip, ix, dt
+        # sequential: pure Python, one core
+        ns = min(N, 20000)
+        ip, ix, dt = O.synth_csr(ns, V, seed=0, law=dlaw)
+        os.sched_setaffinity(0, cores[:1])
+        _, _, secs = O.sequential_score(ip, ix, dt, qi_h[:2], qs_h[:2], ns, k)
+        res["sequential_one_core"] = {
+            "value": 2 / (secs * N / ns), "unit": "queries/s", "cores": 1, "pin": f"cpu {cores[0]}",
+            "sample": f"2 queries x the first {ns:,} docs (index build excluded), scaled to {N:,}",
+            "wall_s": round(secs, 3)}
+    finally:
+        os.sched_setaffinity(0, saved_mask)
+        torch.set_num_threads(saved_threads)
+    res["physical_cores"] = len(cores)
+    res["logical_cpus"] = len(saved_mask)
+    return res
 
 
 def run_ours(args):
@@ -362,18 +468,16 @@ def run_ours(args):
     mads = max_over_ranks(contributions(index, qi))
     peak, peak_src = peaks()
     achieved = balg / (kern_ms * 1e-3) / 1e9
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", f"score_kernel_traffic_config{args.config}.md")
-    if os.path.exists(tp):
-        import re
-        m = re.search(rf"config{args.config}_gpus{world} dram_bytes_per_launch: (\d+)", open(tp).read())
-        if m:
-            traffic = int(m.group(1))
+    traffic, traffic_src = measured_traffic(args.config, world, args.num_docs)
+    if args.head_mode == "tc":
+        traffic, traffic_src = None, "the committed profile covers the CUDA-core scorer"
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gs, gi = (x.cpu().numpy() for x in out)
         cpu = cpu_sample(index, qi, qs, k, gs, gi, args.cpu_seconds)
+        cpu["reference_paths"] = reference_cpu_paths(wl, qi.cpu().numpy(), qs.cpu().numpy(), k,
+                                                     args.cpu_seconds)
 
     sharing = None
     if world > 1:
@@ -385,8 +489,9 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
-    # plan, score, candidate counts, shard merge (+ global merge)
-    launches_per_step = 4 if world == 1 else 5
+    # plan, score, candidate counts, shard merge (+ global merge); the tensor-core mode adds
+    # the query head-weight kernel
+    launches_per_step = (4 if world == 1 else 5) + (1 if args.head_mode == "tc" else 0)
     line = {
         "metric": METRIC,
         "value": B * K / (total_ms * 1e-3),
@@ -417,7 +522,8 @@ def run_ours(args):
         "e2e": {"value": B * K / (e2e_ms * 1e-3), "unit": "queries/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
+                     "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
+                     "source_tag": source_tag(), "peak_source": peak_src,
                      "kernel": "score_kernel", "kernel_ms": kern_ms,
                      "bytes_alg_per_launch": balg, "postings_per_launch": post,
                      "multiply_adds_per_launch": mads},

@@ -314,6 +314,55 @@ __global__ void dedup_count_kernel(int64_t n_rows, const int64_t* __restrict__ i
   if (lane == 0 && drop) atomicAdd(dropped, drop);
 }
 
+// The same count with a bitmap of the vocabulary per warp in shared memory (V bits): an
+// entry repeats an earlier chunk's term if its bit is set, and an earlier lane of its own
+// chunk (match_any); then the chunk's bits are set, and the row's bits cleared at its end.
+// O(nnz) per row; used when 8 warps' bitmaps fit the shared memory.
+__global__ void __launch_bounds__(256)
+dedup_count_bitmap_kernel(int64_t n_rows, int32_t V, const int64_t* __restrict__ indptr,
+                          const int32_t* __restrict__ indices, int32_t* __restrict__ nnz,
+                          unsigned long long* __restrict__ dropped) {
+  extern __shared__ uint32_t bm_all[];
+  const int lane = lane_id(), wid = threadIdx.x >> 5;
+  const int32_t words = (V + 31) >> 5;
+  uint32_t* bm = bm_all + int64_t(wid) * words;
+  for (int32_t i = lane; i < words; i += 32) bm[i] = 0u;
+  __syncwarp();
+  const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
+  unsigned long long drop = 0;
+  for (int64_t r = int64_t(blockIdx.x) * (blockDim.x >> 5) + wid; r < n_rows; r += warps) {
+    const int64_t e0 = indptr[r], e1 = indptr[r + 1];
+    int32_t kept = 0;
+    for (int64_t j0 = e0; j0 < e1; j0 += 32) {
+      const bool valid = j0 + lane < e1;
+      const int32_t t = valid ? indices[j0 + lane] : 0;
+      const bool inv = valid && (t < 0 || t >= V);   // out of range: counted as distinct here,
+                                                     // refused by the index build's count pass
+      const uint32_t bit = 1u << (t & 31);
+      bool dup = valid && !inv && (bm[t >> 5] & bit) != 0u;
+      const uint32_t vmask = __ballot_sync(FULL, valid);
+      const uint32_t peers = __match_any_sync(FULL, valid ? t : int32_t(0x80000000u) + lane) & vmask;
+      dup |= (peers & lanemask_lt()) != 0u;
+      kept += __popc(__ballot_sync(FULL, valid && !dup));
+      __syncwarp();
+      if (valid && !inv) atomicOr(&bm[t >> 5], bit);
+      __syncwarp();
+    }
+    for (int64_t j0 = e0; j0 < e1; j0 += 32) {
+      if (j0 + lane < e1) {
+        const int32_t t = indices[j0 + lane];
+        if (t >= 0 && t < V) bm[t >> 5] = 0u;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      nnz[r] = kept;
+      drop += uint64_t(e1 - e0 - kept);
+    }
+  }
+  if (lane == 0 && drop) atomicAdd(dropped, drop);
+}
+
 // out row r (at new_indptr[r] - new_indptr[0]) = the first occurrence of every term of in
 // row r, in row order, each with the fp32 sum of its occurrences' weights in row order
 // (data and out_data may be null: indices only)
@@ -569,9 +618,9 @@ extern "C" int gsp_index_fill(int64_t n_docs, int32_t V, int32_t block_docs, con
                                ws_bytes, stream);
 }
 
-extern "C" int gsp_csr_dedup_count(int64_t n_rows, const int64_t* indptr, const int32_t* indices,
-                                   int32_t* nnz, int64_t* n_dropped, void* ws, int64_t ws_bytes,
-                                   void* stream) {
+extern "C" int gsp_csr_dedup_count(int64_t n_rows, int32_t V, const int64_t* indptr,
+                                   const int32_t* indices, int32_t* nnz, int64_t* n_dropped, void* ws,
+                                   int64_t ws_bytes, void* stream) {
   GSP_REQUIRE(n_rows >= 0 && indptr && nnz && n_dropped && ws && ws_bytes >= 8, GSP_ERR_ARG,
               "gsp_csr_dedup_count: bad arguments");
   cudaStream_t st = as_stream(stream);
@@ -579,7 +628,14 @@ extern "C" int gsp_csr_dedup_count(int64_t n_rows, const int64_t* indptr, const 
   GSP_CUDA(cudaMemsetAsync(d, 0, 8, st));
   if (n_rows > 0) {
     const int64_t blocks = std::min<int64_t>((n_rows + 7) / 8, int64_t(num_sms()) * 32);
-    dedup_count_kernel<<<unsigned(blocks), 256, 0, st>>>(n_rows, indptr, indices, nnz, d);
+    const int64_t bm_bytes = 8 * int64_t((std::max(V, 1) + 31) / 32) * 4;
+    if (V > 0 && bm_bytes <= 96 * 1024) {
+      if (int rc = ensure_smem(reinterpret_cast<const void*>(dedup_count_bitmap_kernel), int(bm_bytes))) return rc;
+      const int64_t bblocks = std::min<int64_t>((n_rows + 7) / 8, int64_t(num_sms()) * 2);
+      dedup_count_bitmap_kernel<<<unsigned(bblocks), 256, size_t(bm_bytes), st>>>(n_rows, V, indptr, indices, nnz, d);
+    } else {
+      dedup_count_kernel<<<unsigned(blocks), 256, 0, st>>>(n_rows, indptr, indices, nnz, d);
+    }
     GSP_CHECK_LAUNCH();
   }
   unsigned long long h = 0;

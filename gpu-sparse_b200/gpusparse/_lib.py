@@ -96,7 +96,7 @@ def lib() -> ctypes.CDLL:
             "gsp_index_fill_chunk": (ctypes.c_int, [i64, i32, i32, i64, i64, p, p, p, p, p, p, p,
                                                     p, i64, p]),
             "gsp_index_fill_finish": (ctypes.c_int, [i64, i32, p, p, p, p, p, p, i64, p]),
-            "gsp_csr_dedup_count": (ctypes.c_int, [i64, p, p, p, ctypes.POINTER(i64), p, i64, p]),
+            "gsp_csr_dedup_count": (ctypes.c_int, [i64, i32, p, p, p, ctypes.POINTER(i64), p, i64, p]),
             "gsp_csr_dedup_fill": (ctypes.c_int, [i64, p, p, p, p, p, p, p]),
             "gsp_index_quantize": (ctypes.c_int, [i32, i64, p, p, p, p, i32, p, p, p]),
             "gsp_index_head_rows": (ctypes.c_int, [i32, p, p, p, p, p, i32, i64, p, p]),

@@ -113,6 +113,10 @@ def build_streamed(num_docs: int, vocab_size: int, get_chunk, device,
     bounds = [(lo, min(N, lo + step)) for lo in range(0, N, max(step, 1))]
     lib = L.lib()
 
+    # chunks whose count pass found no repeated terms skip the check in the fill pass (the
+    # same rows by contract)
+    clean = set()
+
     def fetch(lo, hi, with_data):
         ip, ix, dt = get_chunk(lo, hi, with_data)
         ip = torch.as_tensor(ip).to(device=device, dtype=torch.int64).contiguous()
@@ -127,7 +131,12 @@ def build_streamed(num_docs: int, vocab_size: int, get_chunk, device,
                                  "weights")
         else:
             dt = None
-        return merge_duplicates(ip, ix, dt)
+        if (lo, hi) in clean:
+            return ip, ix, dt
+        out = merge_duplicates(ip, ix, dt, V)
+        if out[1] is ix and not with_data:
+            clean.add((lo, hi))
+        return out
 
     with torch.cuda.device(device):
         st = L.stream_of(device)
@@ -173,11 +182,12 @@ def build_streamed(num_docs: int, vocab_size: int, get_chunk, device,
     return idx
 
 
-def merge_duplicates(indptr: torch.Tensor, indices: torch.Tensor, data=None):
+def merge_duplicates(indptr: torch.Tensor, indices: torch.Tensor, data=None, vocab_size: int = 0):
     """Device CSR rows with every term once: a term that a row lists more than once keeps
     its first position and the fp32 sum of its weights in row order (the reference keeps
     both entries as postings and its scatter-add sums them per document).  Returns the
-    inputs unchanged when no row repeats a term; ``indptr`` may start above 0."""
+    inputs unchanged when no row repeats a term; ``indptr`` may start above 0.
+    ``vocab_size`` (if known) lets the check use a vocabulary bitmap."""
     n = indptr.numel() - 1
     dev = indptr.device
     lib = L.lib()
@@ -187,7 +197,7 @@ def merge_duplicates(indptr: torch.Tensor, indices: torch.Tensor, data=None):
     dropped = ctypes.c_int64(0)
     ws = L.workspace(8, dev)
     st = L.stream_of(dev)
-    L.check(lib.gsp_csr_dedup_count(n, L.ptr(indptr), L.ptr(indices), L.ptr(nnz),
+    L.check(lib.gsp_csr_dedup_count(n, int(vocab_size), L.ptr(indptr), L.ptr(indices), L.ptr(nnz),
                                     ctypes.byref(dropped), L.ptr(ws), ws.numel(), st),
             "merge duplicate entries")
     if dropped.value == 0:

@@ -125,12 +125,13 @@ int gsp_index_fill_finish(int64_t n_docs, int32_t V, const int64_t* offsets,
  * its place and its weight becomes the fp32 sum of all occurrences' weights in row order.
  * count: nnz[r] = distinct terms of row r (rows [0, n_rows) of indptr, whose first entry
  * need not be 0), *n_dropped (host; the call synchronises) = entries merged away;
- * ws >= 8 bytes of device scratch.  fill: the merged rows at new_indptr (n_rows + 1
+ * ws >= 8 bytes of device scratch; V (the vocabulary size, or 0 if unknown) lets the count
+ * use a bitmap of the vocabulary (terms outside [0, V) count as distinct there).  fill: the merged rows at new_indptr (n_rows + 1
  * entries, e.g. the scan of nnz) relative to new_indptr[0]; data and out_data may both be
  * NULL to merge the indices only. */
-int gsp_csr_dedup_count(int64_t n_rows, const int64_t* indptr, const int32_t* indices,
-                        int32_t* nnz, int64_t* n_dropped, void* ws, int64_t ws_bytes,
-                        void* stream);
+int gsp_csr_dedup_count(int64_t n_rows, int32_t V, const int64_t* indptr,
+                        const int32_t* indices, int32_t* nnz, int64_t* n_dropped, void* ws,
+                        int64_t ws_bytes, void* stream);
 int gsp_csr_dedup_fill(int64_t n_rows, const int64_t* indptr, const int32_t* indices,
                        const float* data, const int64_t* new_indptr, int32_t* out_indices,
                        float* out_data, void* stream);

@@ -18,6 +18,11 @@ What is restated here (reference paths are relative to the GPUSparse checkout):
   canonical summation order documented in ``oracle.c``.
 * ``score_dense_f64``: the exhaustive dense reference
   (``src/remeasure_2026_09.py:238-258``) in fp64.
+* ``dense_reference_topk``: that same dense path as the reference runs it (fp32 ``Q @ D^T``
+  per chunk of densified documents, ``torch.topk`` and a running cat/topk/gather merge),
+  on the CPU -- the CPU baseline the benchmark reports beside the C port.
+* ``sequential_score``: ``cpu_sequential_score`` (``src/gpu_scoring.py:221-259``), the
+  reference's pure-Python posting-list loop.
 * ``synth_*``: the seeded synthetic SPLADE-shaped generator (twin of the GPU one).
 """
 from __future__ import annotations
@@ -427,3 +432,73 @@ def quantize_u8(index: Index):
         r = np.where(st > 0, index.scores / st, 0.0).astype(np.float32)
     q = np.clip(np.rint(r), 0, 255).astype(np.uint8)
     return q, scale
+
+
+# ---------------------------------------------------------------- the reference's CPU paths
+
+def dense_query_matrix(qi: np.ndarray, qs: np.ndarray, V: int) -> np.ndarray:
+    """fp32 [B, V] query matrix (term ids outside [0, V) dropped, repeats summed)."""
+    B, W = qi.shape
+    Q = np.zeros((B, V), dtype=np.float32)
+    ok = (qi >= 0) & (qi < V)
+    rows = np.repeat(np.arange(B), W).reshape(B, W)
+    np.add.at(Q, (rows[ok], qi[ok]), qs[ok].astype(np.float32))
+    return Q
+
+
+def dense_reference_topk(indptr, indices, data, V: int, Q: np.ndarray, k: int, doc_lo: int = 0,
+                         doc_hi: int | None = None, chunk: int = 16384):
+    """``src/remeasure_2026_09.py:238-258`` (dense_reference_topk) on the CPU: for every chunk
+    of documents, densify the chunk, S = Q @ D_chunk^T in fp32, torch.topk of each row, and
+    merge into the running top-k with torch.cat / topk / gather.  The reference densifies
+    200 000 documents per chunk on the GPU; ``chunk`` only bounds the dense block's memory.
+    Covers documents [doc_lo, doc_hi); returns (scores fp32 [B, k'], ids int64 [B, k'])."""
+    import torch
+    doc_hi = len(indptr) - 1 if doc_hi is None else doc_hi
+    Qt = torch.from_numpy(np.ascontiguousarray(Q, dtype=np.float32))
+    nq = Qt.shape[0]
+    best_s = torch.zeros((nq, 0), dtype=torch.float32)
+    best_i = torch.zeros((nq, 0), dtype=torch.long)
+    for start in range(doc_lo, doc_hi, chunk):
+        stop = min(doc_hi, start + chunk)
+        e0, e1 = int(indptr[start]), int(indptr[stop])
+        rows = np.repeat(np.arange(stop - start), np.diff(indptr[start:stop + 1]))
+        Db = torch.zeros((stop - start, V), dtype=torch.float32)
+        Db.index_put_((torch.from_numpy(rows), torch.from_numpy(indices[e0:e1].astype(np.int64))),
+                      torch.from_numpy(data[e0:e1].astype(np.float32)), accumulate=True)
+        sc = Qt @ Db.t()
+        kk = min(k, sc.shape[1])
+        vs, ix = torch.topk(sc, kk, dim=1)
+        best_s = torch.cat([best_s, vs], dim=1)
+        best_i = torch.cat([best_i, ix + start], dim=1)
+        vs2, ix2 = torch.topk(best_s, min(k, best_s.shape[1]), dim=1)
+        best_s, best_i = vs2, torch.gather(best_i, 1, ix2)
+        del Db, sc
+    return best_s.numpy(), best_i.numpy()
+
+
+def sequential_score(indptr, indices, data, qi: np.ndarray, qs: np.ndarray, num_docs: int,
+                     top_k: int = 10):
+    """``cpu_sequential_score`` (``src/gpu_scoring.py:221-259``): a Python dict inverted index
+    of (doc, score) lists, then per query a float32 accumulator filled posting by posting and
+    an argpartition top-k.  Returns the (scores, doc ids) lists and the scoring time in
+    seconds (the index build excluded)."""
+    import time
+    inv = {}
+    for d in range(num_docs):
+        for e in range(int(indptr[d]), int(indptr[d + 1])):
+            inv.setdefault(int(indices[e]), []).append((d, float(data[e])))
+    out_s, out_i = [], []
+    t0 = time.perf_counter()
+    for b in range(qi.shape[0]):
+        doc_scores = np.zeros(num_docs, dtype=np.float32)
+        for t, w in zip(qi[b].tolist(), qs[b].tolist()):
+            if t >= 0 and t in inv:
+                for d, ds in inv[t]:
+                    doc_scores[d] += w * ds
+        kk = min(top_k, num_docs)
+        top = np.argpartition(doc_scores, -kk)[-kk:]
+        top = top[np.argsort(doc_scores[top])[::-1]]
+        out_s.append(doc_scores[top].tolist())
+        out_i.append(top.tolist())
+    return out_s, out_i, time.perf_counter() - t0

@@ -192,9 +192,11 @@ def test_duplicate_doc_term_entries_are_merged():
         check_topk(s.cpu().numpy(), i.cpu().numpy(), S, 500)
 
 
-def test_merge_duplicates_kernel_matches_oracle():
+@pytest.mark.parametrize("vocab", [0, 60])
+def test_merge_duplicates_kernel_matches_oracle(vocab):
     """gsp_csr_dedup_* against the oracle's merge on rows of many lengths (up to 700
-    entries, terms repeated up to 40 times) and a chunk whose indptr starts above 0."""
+    entries, terms repeated up to 40 times) and a chunk whose indptr starts above 0; with
+    the vocabulary size unknown (pairwise check) and known (vocabulary bitmap)."""
     from gpusparse.index import merge_duplicates
     rng = np.random.default_rng(7)
     lens = rng.integers(0, 700, size=400)
@@ -205,12 +207,12 @@ def test_merge_duplicates_kernel_matches_oracle():
     dt = rng.random(int(ip[-1])).astype(np.float32)
     for lo, hi in [(0, 400), (37, 211)]:
         sub_ip = ip[lo:hi + 1]
-        got = merge_duplicates(t(sub_ip), t(ix), t(dt))
+        got = merge_duplicates(t(sub_ip), t(ix), t(dt), vocab)
         exp = O.merge_duplicates(sub_ip - sub_ip[0], ix[sub_ip[0]:sub_ip[-1]], dt[sub_ip[0]:sub_ip[-1]])
         assert np.array_equal(got[0].cpu().numpy(), exp[0])
         assert np.array_equal(got[1].cpu().numpy(), exp[1])
         assert np.array_equal(got[2].cpu().numpy().view(np.uint32), exp[2].view(np.uint32))
-        only_ix = merge_duplicates(t(sub_ip), t(ix), None)
+        only_ix = merge_duplicates(t(sub_ip), t(ix), None, vocab)
         assert np.array_equal(only_ix[1].cpu().numpy(), exp[1]) and only_ix[2] is None
 
 
