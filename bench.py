@@ -98,16 +98,19 @@ def workload(args):
     return c
 
 
+SCORER_SOURCES = ("common.cuh", "score.cu", "score_tc.cuh", "select.cu")
+
+
 def source_tag():
-    """Short hash of the CUDA sources (csrc/*.cu, *.cuh): ties a committed ncu figure to the
-    kernels it was measured on."""
+    """Short hash of the sources the scoring launch is compiled from (csrc/common.cuh,
+    score.cu, score_tc.cuh, select.cu): ties a committed ncu figure to the kernels it was
+    measured on."""
     import hashlib
     d = os.path.join(ROOT, "gpu-sparse_b200", "csrc")
     h = hashlib.sha256()
-    for f in sorted(os.listdir(d)):
-        if f.endswith((".cu", ".cuh")):
-            h.update(f.encode())
-            h.update(open(os.path.join(d, f), "rb").read())
+    for f in SCORER_SOURCES:
+        h.update(f.encode())
+        h.update(open(os.path.join(d, f), "rb").read())
     return h.hexdigest()[:12]
 
 
