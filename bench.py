@@ -78,6 +78,9 @@ def parse():
     ap.add_argument("--head-mode", choices=["auto", "cuda", "tc"], default="auto",
                     help="head terms: the library's choice, the CUDA cores (canonical order) or "
                          "the tensor cores (tcgen05, 3xTF32)")
+    ap.add_argument("--phase-split", action="store_true",
+                    help="also time each step's phases (score, exchange, merge, gather) with "
+                         "CUDA events, max over ranks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="target CPU work of the bounded CPU-baseline sample")
@@ -367,8 +370,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     build_s = time.time() - t0
 
-    def step(qi_d, qs_d):
-        return sharded_score_topk(index, lay, qi_d, qs_d, k)
+    def step(qi_d, qs_d, events=None):
+        return sharded_score_topk(index, lay, qi_d, qs_d, k, events=events)
 
     def barrier():
         if world > 1:
@@ -403,6 +406,21 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     per_step = [ev[j].elapsed_time(ev[j + 1]) for j in range(K)]
+    phases = None
+    if args.phase_split:
+        # separate steps, so the timed ones above carry no extra events
+        acc = {}
+        for _ in range(K):
+            e0_ = torch.cuda.Event(enable_timing=True)
+            e0_.record()
+            evs = []
+            step(qi, qs, events=evs)
+            torch.cuda.synchronize()
+            prev = e0_
+            for name, e in evs:
+                acc[name] = acc.get(name, 0.0) + prev.elapsed_time(e)
+                prev = e
+        phases = {n: max_over_ranks(v / K) for n, v in acc.items()}
     total_ms = max_over_ranks(ev[0].elapsed_time(ev[K]))
     import ctypes
     tot, n = ctypes.c_double(0.0), ctypes.c_int64(0)
@@ -466,6 +484,8 @@ def run_ours(args):
         lat1 = statistics.median(t1)
 
     # ---- roofline of the scoring kernel (this rank's shard)
+    from gpusparse.index import index_memory_stats
+    index_bytes = int(index_memory_stats(index)["total_MB"] * 1e6)
     balg, post = bytes_alg(index, qi, B, min(k, index.num_docs), wd)
     balg = max_over_ranks(balg)
     mads = max_over_ranks(contributions(index, qi))
@@ -515,10 +535,14 @@ def run_ours(args):
                    (" + NCCL all-to-all of query blocks, merge, all-gather" if world > 1 else ""),
                    "l2": "inputs larger than L2 (index >> 126 MB); no flush",
                    "index_build_s": round(build_s, 2),
+                   "index_device_bytes": index_bytes,
+                   **({"exchange": __import__("gpusparse.distributed", fromlist=["x"]).exchange_mode()}
+                      if world > 1 else {}),
                    "head_terms": {"auto": "library choice (CUDA cores)", "cuda": "CUDA cores",
                                   "tc": "tensor cores (tcgen05, 3xTF32)"}[args.head_mode],
                    **({"threshold_sharing": sharing} if sharing else {})},
         "gpu_launches": launches_per_step * K,
+        **({"phases_ms": phases} if phases else {}),
         **({"single_query_latency": {"batch": 1, "k": k, "p50_ms": lat1,
                                      "note": "query 1 of the batch alone, device time"}}
            if lat1 is not None else {}),
@@ -592,7 +616,9 @@ def run_reference(args):
                    "index_build_s": round(build_s, 1)},
         "cpu_baseline": {"value": value, "unit": "queries/s", "cores": nt, "kind": "port",
                          "sample": f"{nq} queries per step against all {N:,} docs",
-                         "cpu_over_wall": round(cpu / max(wall, 1e-9), 2)},
+                         "cpu_over_wall": round(cpu / max(wall, 1e-9), 2),
+                         "threads": nt, "affinity": f"{len(os.sched_getaffinity(0))} logical CPUs",
+                         "physical_cores": len(physical_cores()[0])},
         "e2e": {"value": value, "unit": "queries/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

@@ -217,13 +217,33 @@ def gather_results(scores: torch.Tensor, ids: torch.Tensor, B: int, group=None):
     return s_all[:B], i_all[:B]
 
 
+def exchange_mode() -> str:
+    """``blocks`` (default): one all-to-all of query blocks, each rank merges B/G queries,
+    two all-gathers of the results; ``allgather`` (GSP_EXCHANGE=allgather): one all-gather
+    of every rank's keys, every rank merges the whole batch."""
+    return "allgather" if os.environ.get("GSP_EXCHANGE", "blocks") == "allgather" else "blocks"
+
+
 def sharded_score_topk(index, layout: ShardLayout, query_term_ids: torch.Tensor,
-                       query_term_scores: torch.Tensor, top_k: int, group=None):
-    """Exact global top-k of the batch over all shards; every rank gets the result."""
+                       query_term_scores: torch.Tensor, top_k: int, group=None, events=None):
+    """Exact global top-k of the batch over all shards; every rank gets the result.
+
+    ``events`` (a list, optional) receives (phase name, CUDA event recorded after it) on the
+    current stream: score, exchange, merge, gather -- a diagnostic of where a step's time
+    goes."""
     from .scoring import merge_topk, score_topk
     k = min(int(top_k), layout.num_docs)
+
+    def mark(name):
+        if events is not None:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            events.append((name, e))
+
     if layout.world == 1:
-        return score_topk(index, query_term_ids, query_term_scores, k)
+        out = score_topk(index, query_term_ids, query_term_scores, k)
+        mark("score")
+        return out
     if shared_thresholds_enabled():
         dev = index.device if isinstance(index.device, torch.device) else torch.device(index.device)
         boards = _boards(dev, int(query_term_ids.shape[0]), group)
@@ -235,9 +255,20 @@ def sharded_score_topk(index, layout: ShardLayout, query_term_ids: torch.Tensor,
             _, _, keys = score_topk(index, query_term_ids, query_term_scores, k, with_keys=True)
     else:
         _, _, keys = score_topk(index, query_term_ids, query_term_scores, k, with_keys=True)
+    mark("score")
+    if exchange_mode() == "allgather":
+        allk = gather_candidates(keys, k, group)
+        mark("exchange")
+        out = merge_topk(allk, layout.list_counts(k), k)
+        mark("merge")
+        return out
     blk = exchange_candidates(keys, k, group)
+    mark("exchange")
     s, i = merge_topk(blk, layout.list_counts(k), k)
-    return gather_results(s, i, int(query_term_ids.shape[0]), group)
+    mark("merge")
+    out = gather_results(s, i, int(query_term_ids.shape[0]), group)
+    mark("gather")
+    return out
 
 
 def decode_keys(keys: torch.Tensor):

@@ -336,13 +336,24 @@ def ensure_head(index: GPUInvertedIndex, n_head: int = N_HEAD, head_ids=None) ->
         L.check(L.lib().gsp_index_head_rows(H, L.ptr(ids), L.ptr(index.offsets), L.ptr(lengths),
                                             L.ptr(index.doc_ids), L.ptr(w), code, ld, L.ptr(rows),
                                             L.stream_of(dev)), "head rows")
-        lo = None
-        if code == L.W_F32 and H > 0:
-            lo = torch.empty_like(rows)
-            L.check(L.lib().gsp_index_head_lo(rows.numel(), L.ptr(rows), L.ptr(lo), L.stream_of(dev)),
-                    "head rows")
     index.head_ids, index.head_slot, index.head_rows, index.head_ld = ids, slot, rows, ld
     index.head_wdtype = code
+    index.head_lo = None
+
+
+def ensure_head_lo(index: GPUInvertedIndex) -> None:
+    """The tf32 low parts of fp32 head rows (``head_lo``), which only the tensor-core head
+    mode reads: built on first use in that mode, since they cost as much memory as the rows
+    (4.5 GB at 8.8M documents)."""
+    if getattr(index, "head_lo", None) is not None or getattr(index, "head_rows", None) is None:
+        return
+    if getattr(index, "head_wdtype", L.W_F32) != L.W_F32 or index.head_ids.numel() == 0:
+        return
+    rows = index.head_rows
+    lo = torch.empty_like(rows)
+    with torch.cuda.device(index.device):
+        L.check(L.lib().gsp_index_head_lo(rows.numel(), L.ptr(rows), L.ptr(lo), L.stream_of(index.device)),
+                "head rows")
     index.head_lo = lo
 
 
@@ -391,6 +402,8 @@ def load_index(path, device) -> GPUInvertedIndex:
 def view(index: GPUInvertedIndex) -> L.IndexView:
     ensure_blocks(index)
     ensure_head(index)
+    if L.lib().gsp_get_head_mode() == L.HEAD_TENSOR_CORES:
+        ensure_head_lo(index)
     wd = getattr(index, "weight_dtype", "fp32")
     if wd == "fp32":
         w, code = index.scores, L.W_F32

@@ -1,8 +1,9 @@
-"""The sharded scorer as separate processes, one per GPU, over NCCL (skipped with fewer
-than two GPUs): every rank builds the index of its own document range with the global
+"""The sharded scorer as separate processes, one per GPU, over NCCL, at 2, 4 and 8 ranks
+(each skipped with fewer GPUs): every rank builds the index of its own document range with the global
 head set, and the all-gathered, merged top-k must equal the CPU oracle over the whole
 corpus bit for bit, with the ranks sharing thresholds through IPC-mapped boards (over
-several batches, so both boards of each rank are used) and without."""
+several batches, so both boards of each rank are used) and without, and with the
+one-collective exchange."""
 import os
 import socket
 from datetime import timedelta
@@ -54,6 +55,11 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         s3, i3 = sharded_score_topk(idx, lay, qi, qs, K)
         os.environ.pop("GSP_SHARED_THRESHOLDS")
         assert torch.equal(s3.view(torch.int32), s.view(torch.int32)) and torch.equal(i3, i)
+        # the one-collective exchange (every rank merges the whole batch) gives the same
+        os.environ["GSP_EXCHANGE"] = "allgather"
+        s4, i4 = sharded_score_topk(idx, lay, qi, qs, K)
+        os.environ.pop("GSP_EXCHANGE")
+        assert torch.equal(s4.view(torch.int32), s.view(torch.int32)) and torch.equal(i4, i)
         torch.cuda.synchronize()
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), s=s.cpu().numpy(), i=i.cpu().numpy(),
                  head=idx.head_ids.cpu().numpy())
@@ -62,10 +68,11 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_rank_nccl_shards_equal_oracle(tmp_path):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_nccl_shards_equal_oracle(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
-    world = 2
     mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     res = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     for r in range(1, world):                      # every rank holds the same result
