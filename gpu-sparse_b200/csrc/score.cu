@@ -71,7 +71,10 @@
 
 namespace gsp {
 
-constexpr int kWarps = 8;
+#ifndef GSP_SCORE_WARPS
+#define GSP_SCORE_WARPS 8          // warps per scoring CTA
+#endif
+constexpr int kWarps = GSP_SCORE_WARPS;
 #ifndef GSP_SCORE_CTAS_PER_SM
 #define GSP_SCORE_CTAS_PER_SM 4   // resident scoring CTAs per SM (register budget 65536 / (256 * this))
 #endif
@@ -86,9 +89,10 @@ constexpr int kTile = kBlock * GSP_TILE_BLOCKS;   // documents per scoring tile
 constexpr int kSel = 1024;        // documents one selection pass marks (32 per lane)
 constexpr int kTileBlocksI = GSP_TILE_BLOCKS;
 // the head rows are summed over parts of the tile, 1024 documents each with 80 registers
-// (three CTAs per SM), 512 with 64 (four), 256 with fewer, so that the accumulators and
-// row values of one part fit in registers
-constexpr int kHeadPart = kCtasPerSm >= 5 ? 256 : (kCtasPerSm >= 4 ? 512 : 1024);
+// per thread (768 threads per SM), 512 with 64 (1024 threads), 256 with fewer, so that the
+// accumulators and row values of one part fit in registers
+constexpr int kRegsPerThread = 65536 / (kWarps * 32 * kCtasPerSm);
+constexpr int kHeadPart = kRegsPerThread >= 80 ? 1024 : (kRegsPerThread >= 64 ? 512 : 256);
 constexpr int kHeadParts = kTile / kHeadPart;
 constexpr int kHeadVec = kHeadPart / 128;   // float4 accumulators per lane per part
 constexpr int kLongRun = 24;      // tail windows at least this long are streamed on their own
@@ -136,6 +140,7 @@ struct ScoreParams {
   unsigned long long* item_next;   // next work item (zeroed)
   int32_t* fault;              // a bounded wait ran out (zeroed)
   int32_t wait_limit;          // polls before a wait gives up
+  int32_t jitter_ns;           // > 0: lane 0 sleeps this long at the start of half the items
   // Doc-range shards of one batch scored at the same time (n_shards > 1) share a bound:
   // row s of every shard's board [n_shards, B] holds, per query, a key that shard s has at
   // least kg = ceil(k / n_shards) candidates at or above.  The minimum over the rows is a
@@ -422,8 +427,10 @@ constexpr int kUnroll = 4;   // posting chunks of one run in flight together
 // or 2 in registers; NE = 0: ne entries read from ew).  Every pass issues the loads of
 // kUnroll chunks (predicated past n) before it applies any, so a run costs one memory
 // round trip per 32 * kUnroll postings.  A list holds each document at most once (the
-// index build refuses repeats), so the pass reads all its accumulators, updates them in
-// registers and writes them back without ordering the shared-memory accesses.
+// index build merges repeats), so the pass reads all its accumulators, updates them in
+// registers and writes them back without ordering the shared-memory accesses within it;
+// the warp barrier at the end orders it before the next run, whose lanes may hold the
+// same documents.
 template <typename WT, int NE>
 __device__ __forceinline__ void run_window(const int32_t* __restrict__ pd, const WT* __restrict__ pw,
                                            float scale, int32_t n, int32_t d0i, uint32_t span,
@@ -458,11 +465,13 @@ __device__ __forceinline__ void run_window(const int32_t* __restrict__ pd, const
       if (uint32_t(col[u]) < span) acc[col[u]] = v[u];
     }
   }
+  // the next run may add to the same documents from other lanes: this run's stores first
+  __syncwarp();
 }
 
 // Two consecutive runs of one entry each and at most 64 postings each (A then B, in term
 // order): the loads of both (two chunks each) in flight together, then A's chunks applied,
-// then B's (A and B may share documents).
+// a warp barrier, then B's (A and B may share documents, held by different lanes).
 template <typename WT>
 __device__ __forceinline__ void run_pair(const int32_t* __restrict__ pa, const WT* __restrict__ wa, float sa,
                                          int32_t na, float qa, const int32_t* __restrict__ pb,
@@ -493,6 +502,9 @@ __device__ __forceinline__ void run_pair(const int32_t* __restrict__ pa, const W
     for (int u = 2 * hh; u < 2 * hh + 2; ++u) {
       if (uint32_t(col[u]) < span) acc[col[u]] = v[u];
     }
+    // B's lanes read a document only after A's lanes have stored it (the lanes of a warp
+    // need not run in step between the phases)
+    __syncwarp();
   }
 }
 
@@ -1018,6 +1030,7 @@ score_kernel(const ScoreParams p) {
     if (lane == 0) nit = atomicAdd(p.item_next, 1ull);
     // items stay below 2^31 (make_cfg), so 32-bit division suffices
     const uint32_t it32 = uint32_t(it);
+    if (p.jitter_ns > 0 && lane == 0 && ((it32 * 2654435761u) >> 31) != 0u) __nanosleep(uint32_t(p.jitter_ns));
     const int32_t b = int32_t(it32 / uint32_t(p.q_n));
     const int32_t q = p.q_lo + int32_t(it32 - uint32_t(b) * uint32_t(p.q_n));
     const int64_t pbase = int64_t(q) * p.ecap;
@@ -1075,6 +1088,7 @@ struct Cfg {
 
 int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 std::atomic<int32_t> g_wait_limit{kSpinLimit};
+std::atomic<int32_t> g_jitter_ns{0};
 // How head terms are summed.  The automatic mode uses the CUDA cores: for the fp32 head rows
 // of fp32 and uint8 indexes the tensor-core path measured slower on B200 (see score_tc.cuh),
 // and bf16 rows have no tensor-core path.
@@ -1342,6 +1356,7 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   p.ecap = int32_t(c.ecap);
   p.cap = c.cap;
   p.wait_limit = g_wait_limit.load();
+  p.jitter_ns = g_jitter_ns.load();
   p.cand_stride = c.stride;
   p.n_head_e = reinterpret_cast<int32_t*>(w + c.off_nhe);
   p.head_h = reinterpret_cast<uint16_t*>(w + c.off_hh);
@@ -1473,6 +1488,13 @@ extern "C" int gsp_set_wait_limit(int32_t polls) {
 }
 
 extern "C" int32_t gsp_get_wait_limit(void) { return g_wait_limit.load(); }
+
+extern "C" int gsp_set_schedule_jitter(int32_t ns) {
+  GSP_REQUIRE(ns >= 0 && ns <= 1000000, GSP_ERR_ARG, "gsp_set_schedule_jitter: %d ns outside [0, 1000000]", ns);
+  g_jitter_ns.store(ns);
+  return GSP_OK;
+}
+extern "C" int32_t gsp_get_schedule_jitter(void) { return g_jitter_ns.load(); }
 
 extern "C" int gsp_set_head_mode(int32_t mode) {
   GSP_REQUIRE(mode == GSP_HEAD_AUTO || mode == GSP_HEAD_CUDA_CORES || mode == GSP_HEAD_TENSOR_CORES, GSP_ERR_ARG,

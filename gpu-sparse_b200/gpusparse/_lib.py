@@ -37,7 +37,7 @@ EXPORTS = (
     "gsp_index_quantize", "gsp_index_head_rows", "gsp_index_head_lo", "gsp_set_head_mode",
     "gsp_get_head_mode", "gsp_check_sorted", "gsp_chunk_bounds", "gsp_score_ws_bytes",
     "gsp_score_topk", "gsp_score_topk_noalloc", "gsp_score_topk_shared", "gsp_board_alloc",
-    "gsp_board_free", "gsp_board_open", "gsp_board_close", "gsp_board_clear", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_set_tree_limit", "gsp_get_tree_limit", "gsp_merge_ws_bytes", "gsp_merge_topk",
+    "gsp_board_free", "gsp_board_open", "gsp_board_close", "gsp_board_clear", "gsp_profile_enable", "gsp_profile_collect", "gsp_set_wait_limit", "gsp_get_wait_limit", "gsp_set_schedule_jitter", "gsp_get_schedule_jitter", "gsp_set_tree_limit", "gsp_get_tree_limit", "gsp_merge_ws_bytes", "gsp_merge_topk",
     "gsp_compacted_ws_bytes", "gsp_compacted_topk",
 )
 
@@ -121,6 +121,8 @@ def lib() -> ctypes.CDLL:
             "gsp_profile_enable": (ctypes.c_int, [ctypes.c_int]),
             "gsp_set_wait_limit": (ctypes.c_int, [ctypes.c_int32]),
             "gsp_get_wait_limit": (ctypes.c_int32, []),
+            "gsp_set_schedule_jitter": (ctypes.c_int, [ctypes.c_int32]),
+            "gsp_get_schedule_jitter": (ctypes.c_int32, []),
             "gsp_set_tree_limit": (ctypes.c_int, [i64]),
             "gsp_get_tree_limit": (i64, []),
             "gsp_profile_collect": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double),

@@ -301,6 +301,15 @@ int gsp_profile_enable(int on);
 int gsp_set_wait_limit(int32_t polls);
 int32_t gsp_get_wait_limit(void);
 
+/* Scheduling jitter of the CUDA-core scorer (no reference counterpart; a test control,
+ * default 0 = off): lane 0 of every scoring warp sleeps about `ns` nanoseconds at the start
+ * of half of its work items (a fixed hash of the item picks them), which reshuffles how the
+ * lanes of a warp and the warps of an SM interleave.  Results must not change: the tests
+ * score under it to show that the canonical summation order does not depend on scheduling.
+ * No work is skipped.  Applies to calls issued after it; process-wide; 0 <= ns <= 1000000. */
+int gsp_set_schedule_jitter(int32_t ns);
+int32_t gsp_get_schedule_jitter(void);
+
 /* Small-batch mode (no reference counterpart).  A batch with 256 <= k' <= 1024, at most
  * 24576 (query, 1024-document tile) pairs and per-tile lists of at most `bytes`
  * (B x ceil(n_docs / 1024) x k' x 8; default 256 MiB) skips the shared candidate

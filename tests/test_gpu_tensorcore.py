@@ -167,3 +167,27 @@ def test_config1_batch_1000_on_tensor_cores(wd):
     S = O.score_dense_f64(ip, ix, dt_eff, V, qi_h[few], qs_h[few])
     rec = check_topk(s[few], i[few], S, 1000)
     assert rec == {10: 1.0, 100: 1.0, 1000: 1.0}
+
+
+def test_exhausted_waits_on_tensor_cores_report_a_fault(corpus, gindex):
+    """With a wait limit of 0 the tensor-core kernel's stage, accumulator and unit waits give
+    up at their first poll: the call reports the fault (NaN scores, ids -1) after its copies
+    and products in flight have landed and its tensor memory is released, and the next call
+    on the same context, with the default limit, is correct again."""
+    import gpusparse
+    import gpusparse._lib as L
+    lib = L.lib()
+    ip, ix, dt, oidx = corpus
+    qi, qs = O.synth_queries(130, V, seed=21)
+    default = lib.gsp_get_wait_limit()
+    L.check(lib.gsp_set_wait_limit(0), "wait limit")
+    try:
+        s, i = gpusparse.triton_fused_score(gindex, t(qi), t(qs), top_k=100)
+        torch.cuda.synchronize()
+    finally:
+        L.check(lib.gsp_set_wait_limit(default), "wait limit")
+    assert tc_used(gindex)
+    assert bool(torch.isnan(s).all()) and bool((i == -1).all())
+    s, i = gpusparse.triton_fused_score(gindex, t(qi), t(qs), top_k=100)
+    rs, ri = O.score_topk(oidx, qi, qs, 100, head=gindex.head_ids.cpu().numpy())
+    assert_topk_close(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
