@@ -651,8 +651,11 @@ __device__ __noinline__ uint64_t append_candidates(QueryBuf qb, const float* __r
       }
       __syncwarp();
       if (pos + total <= qb.cap) {
-        __threadfence();
-        if (lane == 0) atomicAdd(qb.done + bsel, total);
+        // the written count, released: the warp barrier above orders every lane's key
+        // stores before lane 0's release, which makes them visible before the count (one
+        // release reduction measured cheaper than a fence and a relaxed add)
+        if (lane == 0)
+          asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(qb.done + bsel), "r"(total) : "memory");
         return 0;
       }
       // this warp crossed the capacity of generation g0
