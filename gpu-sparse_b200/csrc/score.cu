@@ -14,16 +14,21 @@
 //
 // Candidates.  Each query has two candidate buffers used in turn and a keep list of the k
 // best keys found so far, shared by all warps; a 64-bit word (generation << 32 | reserved
-// slots) says which buffer is open (the generation's low bit) and how far it is reserved,
-// and a written counter per buffer counts finished writes.  A warp reserves room for its
-// keys with one atomicAdd on the word, which also tells it the generation; below the
-// capacity it writes the keys and adds their count to the buffer's written counter.  The
-// warp whose reservation crosses the capacity writes its keys into the buffer's spare
-// tail, waits for the previous compaction to finish (it read the other buffer and wrote
-// the keep list), opens the next generation on the other buffer, empty, so that the other
-// warps go on appending there, waits until every earlier reservation of its own
-// generation is written, and then keeps the k largest of that buffer and the keep list as
-// the new keep list and publishes the k-th as the query's threshold.  Warps that reserved
+// slots) says which buffer is open (the generation's low bit) and how far it is reserved.
+// A buffer is all zeros when its generation opens, and a key is never zero, so a slot
+// that holds a key has been written.  A warp reserves room for its keys with one
+// atomicAdd on the word, which also tells it the generation, and below the capacity
+// writes the keys; nothing else (no fence, no counter).  The warp whose reservation
+// crosses the capacity writes its keys into the buffer's spare tail, waits for the
+// previous compaction to finish (it read the other buffer, wrote the keep list and zeroed
+// that buffer), opens the next generation on the other buffer so that the other warps go
+// on appending there, waits until every slot below its own reservation holds a key, and
+// then keeps the k largest of that buffer and the keep list as the new keep list,
+// publishes the k-th as the query's threshold and zeroes every slot its generation used.
+// The zeroing is ordered before any key of the buffer's next generation, two generations
+// on: the compactor fences before it marks the compaction finished, the next crossing
+// warp waits for that mark and fences before it opens the next generation, and a key's
+// slot is known only from the reservation that reads the opened word.  Warps that reserved
 // past the capacity wait only until the next generation is open.
 // Every wait is bounded; one that runs out records a fault, and the merge then reports
 // NaN scores instead of a result.
@@ -134,7 +139,6 @@ struct ScoreParams {
   uint64_t* cand;              // [B, 3, cand_stride]: keep list, buffer 0, buffer 1
   unsigned long long* gthr;    // [B] published lower bound of each query's k-th key (zeroed)
   unsigned long long* rg;      // [B] generation << 32 | reserved slots (zeroed)
-  int32_t* done;               // [B, 2] written slots per buffer (zeroed)
   int32_t* cdone;              // [B] finished compactions (zeroed)
   int32_t* counts;             // [B, 3] final candidates: keep list, buffer 0, buffer 1
   unsigned long long* item_next;   // next work item (zeroed)
@@ -604,13 +608,41 @@ __device__ __forceinline__ bool wait_generation(const unsigned long long* a, uin
   return false;
 }
 
+// Bounded wait until every slot of buf[0, n) holds a key (is not zero); read through L2,
+// kCompactUnroll slots per lane at a time.  Warp-uniform result.
+__device__ __noinline__ bool wait_keys(const uint64_t* buf, int32_t n, int32_t limit) {
+  const int lane = lane_id();
+  bool ok = true;
+  for (int32_t i0 = 0; i0 < n; i0 += 32 * kCompactUnroll) {
+    uint64_t kk[kCompactUnroll];
+#pragma unroll
+    for (int u = 0; u < kCompactUnroll; ++u) {
+      const int32_t i = i0 + 32 * u + lane;
+      kk[u] = i < n ? __ldcg(buf + i) : 1ull;
+    }
+#pragma unroll
+    for (int u = 0; u < kCompactUnroll; ++u) {
+      const volatile unsigned long long* slot =
+          reinterpret_cast<const volatile unsigned long long*>(buf + i0 + 32 * u + lane);
+      for (int32_t w = 0; kk[u] == 0ull && ok; ++w) {
+        if (w >= limit) {
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+        kk[u] = *slot;
+      }
+    }
+  }
+  return __all_sync(FULL, ok);
+}
+
 // Per-query state of the shared candidate buffers.
 struct QueryBuf {
   uint64_t* region;            // keep list, buffer 0, buffer 1, stride keys apart
   int64_t stride;
   unsigned long long* gthr;
   unsigned long long* rg;
-  int32_t* done;               // [2]
   int32_t* cdone;
   int32_t* fault;
   int32_t cap, k;
@@ -650,27 +682,21 @@ __device__ __noinline__ uint64_t append_candidates(QueryBuf qb, const float* __r
         buf[o++] = pack_key(acc[col], dbase + uint32_t(col));
       }
       __syncwarp();
-      if (pos + total <= qb.cap) {
-        // the written count, released: the warp barrier above orders every lane's key
-        // stores before lane 0's release, which makes them visible before the count (one
-        // release reduction measured cheaper than a fence and a relaxed add)
-        if (lane == 0)
-          asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(qb.done + bsel), "r"(total) : "memory");
-        return 0;
-      }
+      // below the capacity the keys themselves mark their slots written
+      if (pos + total <= qb.cap) return 0;
       // this warp crossed the capacity of generation g0
       bool ok = true;
       if (lane == 0) {
-        // the previous compaction read the other buffer and wrote the keep list
+        // the previous compaction read the other buffer, wrote the keep list and zeroed
+        // that buffer
         ok = wait_equal(qb.cdone, int32_t(g0), qb.wait_limit);
-        // open generation g0 + 1 on the other buffer, empty: the other warps go on there
-        atomicExch(qb.done + (bsel ^ 1), 0);
+        // open generation g0 + 1 on the other buffer: the other warps go on there
         __threadfence();
         atomicExch(qb.rg, static_cast<unsigned long long>(g0 + 1u) << 32);
-        // every earlier reservation of generation g0 is written
-        ok = wait_equal(qb.done + bsel, pos, qb.wait_limit) && ok;
-        if (!ok) atomicOr(qb.fault, 1);
       }
+      // every earlier reservation of generation g0 is written: its slots hold keys
+      ok = wait_keys(buf, pos, qb.wait_limit) && __shfl_sync(FULL, int(ok), 0) != 0;
+      if (!ok && lane == 0) atomicOr(qb.fault, 1);
       __syncwarp();
       __threadfence();
       // the k largest of this buffer and the keep list become the keep list
@@ -689,6 +715,10 @@ __device__ __noinline__ uint64_t append_candidates(QueryBuf qb, const float* __r
       // the shared-bound key, read while this warp still owns the keep list: the next
       // compaction of this query, which rewrites it, waits for the cdone below
       const uint64_t pc = qb.kg > 0 ? warp_select(keep, qb.k, qb.kg, hist) : 0ull;
+      // this generation's slots back to zero for the buffer's next generation
+      for (int32_t j = lane; j < n; j += 32) buf[j] = 0ull;
+      __syncwarp();
+      __threadfence();
       if (lane == 0) {
         atomicMax(qb.gthr, (unsigned long long)t);
         __threadfence();
@@ -807,16 +837,19 @@ __device__ __noinline__ void tile_topk(const float* __restrict__ acc, uint32_t s
 }
 
 // Final candidate counts of every query: the keep list (k once a compaction happened) and
-// the open buffer (its written keys); the other buffer was compacted into the keep list.
-__global__ void final_counts_kernel(int32_t B, int32_t k, const unsigned long long* __restrict__ rg,
-                                    const int32_t* __restrict__ done, const int32_t* __restrict__ cdone,
-                                    int32_t* __restrict__ counts) {
+// the open buffer (its reserved slots, all written once the scorer has ended; a generation
+// reserved past the capacity was compacted and closed by its crossing warp); the other
+// buffer was compacted into the keep list.
+__global__ void final_counts_kernel(int32_t B, int32_t k, int32_t cap, const unsigned long long* __restrict__ rg,
+                                    const int32_t* __restrict__ cdone, int32_t* __restrict__ counts) {
   const int32_t q = blockIdx.x * blockDim.x + threadIdx.x;
   if (q >= B) return;
-  const int b = int((rg[q] >> 32) & 1ull);
+  const unsigned long long w = rg[q];
+  const int b = int((w >> 32) & 1ull);
+  const int32_t n = int32_t(min(uint32_t(w), uint32_t(cap)));
   counts[3 * q + 0] = cdone[q] > 0 ? k : 0;
-  counts[3 * q + 1] = b == 0 ? done[2 * q] : 0;
-  counts[3 * q + 2] = b == 1 ? done[2 * q + 1] : 0;
+  counts[3 * q + 1] = b == 0 ? n : 0;
+  counts[3 * q + 2] = b == 1 ? n : 0;
 }
 
 // Steps 2 and 3 of one work item (query q, tile b), after the head terms are in acc: the
@@ -993,7 +1026,7 @@ __device__ __forceinline__ void item_tail_select(const ScoreParams& p, const int
     const uint32_t m = mark_tile(acc + h * kSel, lane, sp, thr);
     if (__any_sync(FULL, m != 0u)) {
       QueryBuf qb{p.cand + int64_t(q) * 3 * p.cand_stride, p.cand_stride, p.gthr + q, p.rg + q,
-                  p.done + 2 * q, p.cdone + q, p.fault, p.cap, p.k, p.wait_limit, p.kg};
+                  p.cdone + q, p.fault, p.cap, p.k, p.wait_limit, p.kg};
       const uint64_t pub =
           append_candidates(qb, acc + h * kSel, sp, uint32_t(p.doc_base + d0i + h * kSel), hist, thr, m);
       // this shard's row of every board: local, then the peers' (remote reductions over
@@ -1131,9 +1164,9 @@ void set_layout(Cfg& c, int64_t B) {
   c.off_entw = o; o = align256(o + E * 4);
   c.off_cand = o; o = align256(o + (c.dense ? 0 : B * 3 * c.stride * 8));
   c.off_counts = o; o = align256(o + B * 3 * 4);
-  // cleared by every call: thresholds [B] u64, reservation words [B] u64, written
-  // counters [B, 2], finished compactions [B], item counter u64, fault flag
-  c.off_zero = o; c.zero_bytes = align8(2 * B * 8 + 3 * B * 4) + 24; o = align256(o + c.zero_bytes);
+  // cleared by every call: thresholds [B] u64, reservation words [B] u64, finished
+  // compactions [B], item counter u64, fault flag
+  c.off_zero = o; c.zero_bytes = align8(2 * B * 8 + B * 4) + 24; o = align256(o + c.zero_bytes);
   if (c.tc) {
     c.qh_rows = (B + tc::kUnitQ - 1) / tc::kUnitQ * tc::kUnitQ;
     c.off_qh = o; o = align256(o + c.qh_rows * 128 * 4);
@@ -1375,10 +1408,9 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
   char* z = w + c.off_zero;
   p.gthr = reinterpret_cast<unsigned long long*>(z);
   p.rg = reinterpret_cast<unsigned long long*>(z + B * 8);
-  p.done = reinterpret_cast<int32_t*>(z + 2 * B * 8);
-  p.cdone = p.done + 2 * B;
+  p.cdone = reinterpret_cast<int32_t*>(z + 2 * B * 8);
   p.counts = reinterpret_cast<int32_t*>(w + c.off_counts);
-  p.item_next = reinterpret_cast<unsigned long long*>(z + align8(2 * B * 8 + 3 * B * 4));
+  p.item_next = reinterpret_cast<unsigned long long*>(z + align8(2 * B * 8 + B * 4));
   p.fault = reinterpret_cast<int32_t*>(p.item_next + 1);
   unsigned long long* unit_next = p.item_next + 2;
   GSP_REQUIRE(n_shards >= 1 && n_shards <= kMaxPeers + 1 && shard >= 0 && shard < n_shards &&
@@ -1401,6 +1433,12 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
     GSP_REQUIRE(r >= p.n_peers || p.peer_thr[r], GSP_ERR_ARG, "gsp_score_topk_shared: null peer board %d", r);
   }
   GSP_CUDA(cudaMemsetAsync(z, 0, size_t(c.zero_bytes), st));
+  if (!c.tree && !c.dense && B > 0) {
+    // both candidate buffers of every query start empty (all zeros); the keep lists are
+    // written before they are read
+    GSP_CUDA(cudaMemset2DAsync(p.cand + c.stride, size_t(3 * c.stride * 8), 0, size_t(2 * c.stride * 8), size_t(B),
+                               st));
+  }
 
   const size_t plan_smem = size_t(c.npow2) * 8;
   rc = ensure_smem(reinterpret_cast<const void*>(plan_kernel), int(plan_smem));
@@ -1477,7 +1515,7 @@ static int score_with_cfg(const gsp_index_view* ix, const int32_t* qi, const flo
       n_in = groups;
     }
   }
-  final_counts_kernel<<<unsigned((B + 255) / 256), 256, 0, st>>>(int32_t(B), int32_t(c.kk), p.rg, p.done,
+  final_counts_kernel<<<unsigned((B + 255) / 256), 256, 0, st>>>(int32_t(B), int32_t(c.kk), int32_t(c.cap), p.rg,
                                                                  p.cdone, p.counts);
   GSP_CHECK_LAUNCH();
   return merge_topk_device(p.cand, B, 3, 3 * c.stride, c.stride, p.counts, 3, nullptr, c.kk, out_scores,
