@@ -387,13 +387,15 @@ __device__ uint64_t warp_select(const uint64_t* __restrict__ buf, int32_t n, int
   return prefix;
 }
 
-// Keep exactly the k largest keys of buf[0..n) (n > k, keys distinct) in place (stable)
-// and return the smallest key value that is kept-or-better.
-__device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t k,
-                                 uint32_t* __restrict__ hist) {
+// Write exactly the k largest keys of buf[0..n) (n > k, keys distinct) to dst[0..k) in
+// buffer order and return the smallest key value that is kept-or-better.  dst may be buf
+// itself (in place: the writes never pass the loaded chunks) or an array that does not
+// overlap it.
+__device__ uint64_t warp_compact(const uint64_t* buf, int32_t n, int32_t k, uint32_t* __restrict__ hist,
+                                 uint64_t* dst) {
   const int lane = lane_id();
   const uint64_t prefix = warp_select(buf, n, k, hist);
-  // stable in-place compaction of keys >= prefix (writes never pass the loaded chunks)
+  // stable compaction of keys >= prefix
   int32_t out = 0;
   for (int32_t i0 = 0; i0 < n; i0 += 32 * kCompactUnroll) {
     uint64_t kk[kCompactUnroll];
@@ -407,7 +409,7 @@ __device__ uint64_t warp_compact(uint64_t* __restrict__ buf, int32_t n, int32_t 
     for (int u = 0; u < kCompactUnroll; ++u) {
       const bool keep = i0 + 32 * u + lane < n && kk[u] >= prefix;
       const uint32_t bal = __ballot_sync(FULL, keep);
-      if (keep) buf[out + __popc(bal & lanemask_lt())] = kk[u];
+      if (keep) dst[out + __popc(bal & lanemask_lt())] = kk[u];
       out += __popc(bal);
     }
   }
@@ -703,13 +705,27 @@ __device__ __noinline__ uint64_t append_candidates(QueryBuf qb, const float* __r
       int32_t n = pos + total;
       uint64_t* __restrict__ keep = qb.region;
       if (g0 > 0) {
-        for (int32_t j = lane; j < qb.k; j += 32) buf[n + j] = __ldcg(keep + j);
+        // the keep list appended behind the buffer's keys, kCompactUnroll loads per lane in
+        // flight
+        for (int32_t j0 = 0; j0 < qb.k; j0 += 32 * kCompactUnroll) {
+          uint64_t kk[kCompactUnroll];
+#pragma unroll
+          for (int u = 0; u < kCompactUnroll; ++u) {
+            const int32_t j = j0 + 32 * u + lane;
+            kk[u] = j < qb.k ? __ldcg(keep + j) : 0ull;
+          }
+#pragma unroll
+          for (int u = 0; u < kCompactUnroll; ++u) {
+            const int32_t j = j0 + 32 * u + lane;
+            if (j < qb.k) buf[n + j] = kk[u];
+          }
+        }
         n += qb.k;
         __syncwarp();
         __threadfence();
       }
-      const uint64_t t = warp_compact(buf, n, qb.k, hist);
-      for (int32_t j = lane; j < qb.k; j += 32) keep[j] = __ldcg(buf + j);
+      // the k largest straight into the keep list (its old keys are in buf now)
+      const uint64_t t = warp_compact(buf, n, qb.k, hist, keep);
       __syncwarp();
       __threadfence();
       // the shared-bound key, read while this warp still owns the keep list: the next
