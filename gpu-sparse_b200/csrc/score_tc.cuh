@@ -32,7 +32,7 @@
 // tensor memory is released.
 //
 // Measured on B200 (config 2: 8.8M documents, 1000 queries, k = 1000) this path is slower
-// than the CUDA-core head phase (48.9 against 35.1 ms per batch), which is why the automatic
+// than the CUDA-core head phase (48.2 against 33.7 ms per batch), which is why the automatic
 // head mode keeps fp32 on the CUDA cores; see gsp_set_head_mode.  The operand stream is the
 // limit: a unit's head rows (hi and lo, 1 MB) arrive through TMA at about 20 bytes per clock
 // per SM whatever the number of boxes in flight (about 5.9 TB/s over the GPU, L2-resident or
