@@ -71,3 +71,21 @@ def test_small_batch_tree_mode_bit_exact_under_jitter(jitter):
                                         top_k=k)
     rs, ri = O.score_topk(O.build_index(ip, ix, dt, V), qi, qs, k, head=g.head_ids.cpu().numpy())
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
+
+
+@pytest.mark.parametrize("k", [256, 600])
+def test_frequent_compactions_bit_exact_under_jitter(jitter, shared_buffers_only, k):
+    """Small k over 200K documents through the shared candidate buffers: each query's buffer
+    fills every tile or two early on, so generations open, compact and are zeroed back to
+    back while other warps append, under the jitter."""
+    import gpusparse
+    N, B = 200_000, 96
+    ip, ix, dt = O.synth_csr(N, V, seed=7)
+    g = gpusparse.build_from_csr_tensors(*(torch.from_numpy(a).to(DEV) for a in (ip, ix, dt)), V, DEV)
+    qi, qs = O.synth_queries(B, V, seed=8)
+    oidx = O.build_index(ip, ix, dt, V)
+    rs, ri = O.score_topk(oidx, qi, qs, k, head=g.head_ids.cpu().numpy())
+    for _ in range(2):
+        s, i = gpusparse.triton_fused_score(g, torch.from_numpy(qi).to(DEV), torch.from_numpy(qs).to(DEV),
+                                            top_k=k)
+        assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
