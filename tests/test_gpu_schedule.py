@@ -39,7 +39,7 @@ def test_jitter_control_validates():
     assert lib.gsp_get_schedule_jitter() == 0
 
 
-@pytest.mark.parametrize("wd", ["fp32", "u8"])
+@pytest.mark.parametrize("wd", ["fp32", "u8", "bf16"])
 def test_config1_batch_bit_exact_under_jitter(jitter, wd):
     """Config 1 (1M documents, 1000 queries, k = 1000), the whole batch, shared candidate
     buffers."""
@@ -55,6 +55,8 @@ def test_config1_batch_bit_exact_under_jitter(jitter, wd):
     if wd == "u8":
         q, scale = O.quantize_u8(oidx)
         w = O.dequantize_u8(q, scale, oidx.offsets, oidx.lengths, oidx.padded_lengths)
+    elif wd == "bf16":
+        w = torch.from_numpy(oidx.scores).bfloat16().float().numpy()
     rs, ri = O.score_topk(oidx, qi.cpu().numpy(), qs.cpu().numpy(), k, weights=w,
                           head=g.head_ids.cpu().numpy())
     assert_bit_exact(s.cpu().numpy(), i.cpu().numpy(), rs, ri)
